@@ -1,0 +1,432 @@
+"""Benchmark of the TarMAC attention core on B200 (one JSON line on stdout).
+
+Workload (the fused score-then-select vs dense
+sweep): fused top-k attention, B=1024 episodes per GPU, N=512 agents, d=16,
+k=2, fp32, Q/K/V i.i.d. N(0,1), diagonal excluded, lowest index on ties.
+One step = one call of the fused top-k kernel over the whole batch. Inputs
+rotate over 4 seeded sets (4 x 96 MiB of Q/K/V, larger than the 126 MB L2).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1: launched by torchrun, one rank per GPU; episodes are sharded (weak
+scaling: B per GPU fixed), no data-path collective; barrier + synchronize
+around the timed region, elapsed time = max over ranks.
+
+``value`` is agent-rows/s over all GPUs with inputs resident in HBM; ``e2e``
+is the same metric through the reference-facing call
+(src.kernels.fused_topk_attention.fused_topk_attention_tiled) with pinned
+host buffers and the host<->device copies inside the timed region.
+``--impl reference`` times the CPU port of the reference's eager path
+(oracle/, fp32) on the host cores instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO), str(REPO / "topk-tarmac_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+B_PER_GPU, N_AGENTS, HEAD_D, TOPK = 1024, 512, 16, 2
+N_SETS = 4
+SEED = 1234 + 7 * N_AGENTS + HEAD_D  # the reference's sweep seed
+# the reference's published fused top-k at this config (RTX PRO 6000, sm_120,
+# results/attention_core_batch.json): 837.7 us per step
+REF_PUBLISHED_US = 837.7
+
+
+def log(*a) -> None:
+    print(*a, file=sys.stderr, flush=True)
+
+
+def _peaks() -> dict:
+    f = REPO / "MEASURED_PEAKS.json"
+    if f.exists():
+        d = json.loads(f.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks: NVML polled from a thread during the timed region (read-only)
+# ---------------------------------------------------------------------------
+
+_REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting",
+            0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x10: "sync_boost",
+            0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+
+class ClockSampler:
+    def __init__(self, index: int, period_s: float = 0.02):
+        self.index, self.period = index, period_s
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(
+                self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report that instead of clocks
+            self._nv = None
+            self.error = f"{type(e).__name__}: {e}"
+
+    def _run(self):
+        nv = self._nv
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                try:
+                    rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except Exception:
+                    rs = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                self.samples.append((int(mhz), int(rs)))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+
+    def summary(self) -> dict:
+        if self._nv is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [],
+                    "note": getattr(self, "error", "nvml unavailable")}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [],
+                    "samples": 0}
+        mhz = [m for m, _ in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        names = [n for b, n in _REASONS.items() if bits & b and b != 0x1]
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": names, "samples": len(self.samples),
+                "sm_mhz_min": min(mhz)}
+
+
+# ---------------------------------------------------------------------------
+# the reference arm: the CPU port of the reference's eager path
+# ---------------------------------------------------------------------------
+
+def _cpu_threads() -> int:
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info()
+             if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def cpu_baseline(episodes: int, budget_s: float, reps_min: int = 1) -> dict:
+    """Time oracle.topk_attention(exact=False) — the reference's eager fp32
+    algorithm restated in numpy — on a sample of ``episodes`` episodes of the
+    workload, repeated for about ``budget_s`` seconds; best rate wins."""
+    import numpy as np
+    import torch
+
+    import oracle
+    g = torch.Generator().manual_seed(SEED)
+    q, k, v = (torch.randn(episodes, N_AGENTS, HEAD_D, generator=g).numpy()
+               for _ in range(3))
+    oracle.topk_attention(q[:1], k[:1], v[:1], TOPK, exact=False, want_mask=False)
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < reps_min or time.perf_counter() < t_end:
+        t0 = time.perf_counter()
+        oracle.topk_attention(q, k, v, TOPK, exact=False, want_mask=False)
+        times.append(time.perf_counter() - t0)
+    best = min(times)
+    return {"value": episodes * N_AGENTS / best, "unit": "agent-rows/s",
+            "cores": _cpu_threads(), "kind": "port",
+            "sample": (f"{episodes} episodes of B={B_PER_GPU} N={N_AGENTS} "
+                       f"d={HEAD_D} k={TOPK} fp32, best of {len(times)} "
+                       f"repetitions (numpy port of the reference's eager "
+                       f"top-k path, oracle/tarmac_oracle.py)"),
+            "seconds_per_sample": best}
+
+
+def run_reference(args) -> int:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    # size each step so the whole --warmup/--steps run stays near a minute
+    cal = cpu_baseline(1, 0.0)
+    per_ep = cal["seconds_per_sample"]
+    total = max(1, args.steps + args.warmup)
+    eps = int(max(1, min(64, 60.0 / (total * per_ep))))
+    import numpy as np
+    import torch
+
+    import oracle
+    g = torch.Generator().manual_seed(SEED)
+    q, k, v = (torch.randn(eps, N_AGENTS, HEAD_D, generator=g).numpy()
+               for _ in range(3))
+    for _ in range(args.warmup):
+        oracle.topk_attention(q, k, v, TOPK, exact=False, want_mask=False)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.topk_attention(q, k, v, TOPK, exact=False, want_mask=False)
+    el = time.perf_counter() - t0
+    rate = eps * N_AGENTS * args.steps / el
+    line = {
+        "impl": "reference", "metric": "agent-rows/s (fused top-k attention core)",
+        "value": rate, "unit": "agent-rows/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * el / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic", "config": _config(args.gpus),
+        "cpu_baseline": {"value": rate, "unit": "agent-rows/s",
+                         "cores": _cpu_threads(), "kind": "port",
+                         "sample": f"{eps} episodes per step (of B={B_PER_GPU}"
+                                   f" N={N_AGENTS} d={HEAD_D} k={TOPK})"},
+        "e2e": {"value": rate, "unit": "agent-rows/s",
+                "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+
+def _config(n: int) -> dict:
+    return {"workload": (f"C2 fused score-then-select top-k, B={B_PER_GPU}/GPU "
+                         f"N={N_AGENTS} d={HEAD_D} k={TOPK} fp32, lowest-index "
+                         "ties"),
+            "B_per_gpu": B_PER_GPU, "N": N_AGENTS, "d": HEAD_D, "k": TOPK,
+            "l2": f"inputs larger than L2: {N_SETS} rotating input sets of "
+                  f"{3 * B_PER_GPU * N_AGENTS * HEAD_D * 4 / 2**20:.0f} MiB",
+            "parallelism": f"episode-sharded x{n} (no collective)"}
+
+
+def _time_loop(fn, steps: int, stream) -> float:
+    import torch
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for s in range(steps):
+        fn(s)
+    e1.record(stream)
+    e1.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def _fp32_peak(dev) -> float:
+    """Measured fp32 (TF32 off) cuBLAS GEMM TFLOP/s: the FFMA roof the fp32
+    top-k kernel is bound by (not a tensor-core figure)."""
+    import torch
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        n = 8192
+        a = torch.randn(n, n, device=dev)
+        b = torch.randn(n, n, device=dev)
+        for _ in range(2):
+            a @ b
+        torch.cuda.synchronize(dev)
+        best = float("inf")
+        for _ in range(5):
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record()
+            a @ b
+            e1.record()
+            e1.synchronize()
+            best = min(best, e0.elapsed_time(e1))
+        del a, b
+        return 2 * n ** 3 / (best * 1e-3) / 1e12
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+
+
+def run_ours(args) -> int:
+    import torch
+
+    from tarmac_b200 import ops, shard
+    from src.kernels.fused_topk_attention import fused_topk_attention_tiled
+
+    rank, local, world = shard.env_world()
+    if world != args.gpus:
+        log(f"note: --gpus {args.gpus} but WORLD_SIZE={world}; using {world}")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    multi = shard.init("nccl", timeout_s=300)
+
+    B, N, d, k = B_PER_GPU, N_AGENTS, HEAD_D, TOPK
+    g = torch.Generator().manual_seed(SEED + 7919 * rank)
+    sets = []
+    for _ in range(N_SETS):
+        sets.append([torch.randn(B, N, d, generator=g).to(dev) for _ in range(3)])
+    stream = torch.cuda.current_stream(dev)
+
+    def step(s):
+        q, kk, v = sets[s % N_SETS]
+        ops.topk_attention(q, kk, v, k)
+
+    def dense_step(s):
+        q, kk, v = sets[s % N_SETS]
+        ops.dense_attention(q, kk, v)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize(dev)
+
+    # -- timed region --------------------------------------------------------
+    shard.barrier(dev)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev.index) as clk:
+        ms = _time_loop(step, args.steps, stream)
+    torch.cuda.synchronize(dev)
+    shard.barrier(dev)
+    ms_max = shard.max_over_ranks(ms, dev)
+    per_step_ms = ms_max / args.steps
+    rows = B * N * world
+    value = rows / (per_step_ms * 1e-3)
+    kernel_ms = ms / args.steps  # one launch of our kernel per step
+
+    # -- dense kernel at the same config (top-k / dense ratio) ---------------
+    for s in range(3):
+        dense_step(s)
+    dsteps = max(10, args.steps // 4)
+    dms = _time_loop(dense_step, dsteps, stream) / dsteps
+    dms = shard.max_over_ranks(dms, dev)
+
+    # -- end to end through the reference-facing call, host buffers ----------
+    qh, kh, vh = (t.cpu().pin_memory() for t in sets[0])
+    oh = torch.empty_like(qh).pin_memory()
+    qd, kd, vd = (torch.empty_like(t) for t in sets[0])
+
+    def e2e_step(s):
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        out = fused_topk_attention_tiled(qd, kd, vd, k)
+        oh.copy_(out, non_blocking=True)
+
+    for s in range(3):
+        e2e_step(s)
+    torch.cuda.synchronize(dev)
+    esteps = max(5, min(args.steps, 200))
+    shard.barrier(dev)
+    ems = _time_loop(e2e_step, esteps, stream) / esteps
+    ems = shard.max_over_ranks(ems, dev)
+    e2e_value = rows / (ems * 1e-3)
+
+    # -- sweep of the C2 grid (informational, warm L2) -----------------------
+    sweep = []
+    if rank == 0 and not args.no_sweep:
+        for n_ in (32, 64, 128, 256, 384, 512):
+            gs = torch.Generator().manual_seed(1234 + 7 * n_ + d)
+            q_, k_, v_ = (torch.randn(B, n_, d, generator=gs).to(dev) for _ in range(3))
+            reps = 30
+            row = {"N": n_}
+            for kk_ in (1, 2, 4):
+                ops.topk_attention(q_, k_, v_, kk_)
+                t = _time_loop(lambda s: ops.topk_attention(q_, k_, v_, kk_), reps,
+                               stream) / reps
+                row[f"topk_k{kk_}_us"] = round(1e3 * t, 2)
+            ops.dense_attention(q_, k_, v_)
+            t = _time_loop(lambda s: ops.dense_attention(q_, k_, v_), reps, stream) / reps
+            row["dense_us"] = round(1e3 * t, 2)
+            sweep.append(row)
+
+    fp32_tf = _fp32_peak(dev) if rank == 0 else None
+    if multi:
+        shard.barrier(dev)
+    if rank != 0:
+        shard.shutdown()
+        return 0
+
+    peaks = _peaks()
+    alg_bytes = 4 * B * N * d * 4                      # q, k, v read; out written
+    alg_flops = 2 * B * N * N * d + 2 * B * N * k * d  # scores + aggregation
+    achieved_gbs = alg_bytes / (kernel_ms * 1e-3) / 1e9
+    achieved_tf = alg_flops / (kernel_ms * 1e-3) / 1e12
+    line = {
+        "metric": "agent-rows/s (fused top-k attention core)",
+        "value": value, "unit": "agent-rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": per_step_ms, "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": value / (B * N / (REF_PUBLISHED_US * 1e-6)),
+        "vs_baseline_ref": {"us_per_step": REF_PUBLISHED_US,
+                            "hardware": "RTX PRO 6000 Blackwell (sm_120), 1 GPU",
+                            "source": "results/attention_core_batch.json"},
+        "dtype": "f32", "data": "synthetic",
+        "config": _config(world),
+        "us_per_step": 1e3 * per_step_ms,
+        "dense_us_per_step": 1e3 * dms,
+        "topk_over_dense": per_step_ms / dms,
+        "gpu_launches": args.steps,
+        "e2e": {"value": e2e_value, "unit": "agent-rows/s",
+                "h2d_bytes_per_step": 3 * B * N * d * 4,
+                "d2h_bytes_per_step": B * N * d * 4,
+                "us_per_step": 1e3 * ems},
+        "roofline": {"bound": "hbm", "achieved": achieved_gbs,
+                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": achieved_gbs / peaks["hbm_gbs"],
+                     "traffic": args.traffic, "peak_src": peaks["src"]},
+        "roofline_compute": {"bound": "fp32_ffma", "achieved": achieved_tf,
+                             "peak": fp32_tf, "unit": "TFLOP/s",
+                             "frac": achieved_tf / fp32_tf if fp32_tf else None,
+                             "peak_src": "measured: cuBLAS fp32 GEMM 8192^3, "
+                                         "TF32 off, this run"},
+        "clocks": clk.summary(),
+        "sweep_c2_us": sweep,
+    }
+    if world == 1 and not args.no_cpu:
+        line["cpu_baseline"] = cpu_baseline(args.cpu_episodes, args.cpu_seconds)
+    print(json.dumps(line), flush=True)
+    shard.shutdown()
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser(description=__doc__,
+                                 formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--cpu-episodes", type=int, default=16)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--traffic", type=float, default=None,
+                    help="ncu dram bytes per launch of the top-k kernel")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,168 @@
+/*
+ * tarmac_b200.h — C ABI of the B200 (sm_100a) TarMAC attention core.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream
+ * handle (passed as void*, it is a cudaStream_t; NULL means the legacy default
+ * stream). Nothing is allocated inside the library: the caller owns every
+ * buffer. Every call is asynchronous on the given stream and returns a status
+ * code (TARMAC_OK or one of the TARMAC_ERR_* values below) describing argument
+ * validation and the launch; tarmac_strerror() turns a code into text.
+ *
+ * Tensor layout. Q, K, V and the output O are [B, N, d] arrays of the dtype
+ * named by `dtype` (TARMAC_F32 or TARMAC_BF16) whose innermost (d) stride is
+ * 1. `strides` points at eight int64 element strides
+ *     { q_b, q_n, k_b, k_n, v_b, v_n, o_b, o_n }
+ * (batch stride, then row stride, for Q, K, V, O), or is NULL for contiguous
+ * [B, N, d] arrays. Base pointers and every stride times the element size must
+ * be multiples of 16 bytes when d * element size is a multiple of 16 bytes
+ * (TARMAC_ERR_ALIGN otherwise); other d use a scalar path with no alignment
+ * rule.
+ *
+ * Semantics shared by every attention entry point (restated from the
+ * reference's eager path, src/kernels/fused_topk_attention.py:390-402):
+ *   s[b,i,j] = (q[b,i,:] . k[b,j,:]) * scale, the diagonal j == i excluded;
+ *   softmax over the retained peers of row i; out[b,i,:] = sum_j w_ij v[b,j,:].
+ * Scores and accumulation are fp32 for both dtypes (bf16 inputs are widened).
+ *
+ * Row-count and width limits: 2 <= N, 1 <= d <= 128.
+ */
+#ifndef TARMAC_B200_H
+#define TARMAC_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden default visibility; everything declared in
+ * this header is exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+/* ---- status codes -------------------------------------------------------- */
+#define TARMAC_OK 0
+#define TARMAC_ERR_NULL 1       /* a required pointer is NULL                 */
+#define TARMAC_ERR_SHAPE 2      /* B, N or d outside the supported range      */
+#define TARMAC_ERR_DTYPE 3      /* dtype is not TARMAC_F32 / TARMAC_BF16       */
+#define TARMAC_ERR_TOPK 4       /* k outside [1, N-1] or above the path limit */
+#define TARMAC_ERR_N_TOO_LARGE 5 /* N above the resident-row limit (1024)     */
+#define TARMAC_ERR_ALIGN 6      /* pointer or stride breaks the 16-byte rule  */
+#define TARMAC_ERR_MODE 7       /* unknown selection mode / unsupported combo */
+#define TARMAC_ERR_LAUNCH 8     /* the CUDA launch itself failed              */
+#define TARMAC_ERR_BITS 9       /* Morton bits outside [1, 16]                */
+
+/* ---- element types ------------------------------------------------------- */
+#define TARMAC_F32 0
+#define TARMAC_BF16 1
+
+/* ---- selection modes of tarmac_topk_attention ---------------------------- */
+/* Rank order is score descending; the modes differ only at an exact tie with
+ * the k-th retained score. */
+#define TARMAC_SELECT_ARGMAX 0    /* lowest index wins a tie (k argmax rounds,
+                                     fused_topk_attention.py:275-284)         */
+#define TARMAC_SELECT_THRESHOLD 1 /* every peer tied with the k-th score is
+                                     kept, so a tie retains more than k
+                                     (fused_topk_attention.py:180-194)       */
+#define TARMAC_SELECT_SORT 2      /* highest index wins a tie (descending sort
+                                     of (key<<32)|idx,
+                                     fused_topk_attention.py:469-474)        */
+
+/* ---- library identity ---------------------------------------------------- */
+/* ABI version of this header; bumped on any signature change. */
+#define TARMAC_ABI_VERSION 1
+int tarmac_abi_version(void);
+/* Static text for a status code (never NULL). */
+const char *tarmac_strerror(int status);
+
+/* ---- dense attention ----------------------------------------------------- */
+/* Softmax over all N-1 peers (diagonal excluded), online softmax, no score
+ * matrix written. Replaces fused_dense_attention and its kernel
+ * _flash_dense_kernel (src/kernels/fused_dense_attention.py:38-152); the
+ * eager forms are dense_unfused / dense_fused
+ * (scripts/bench_attention_core.py:74-82). */
+int tarmac_dense_attention(const void *q, const void *k, const void *v,
+                           void *out, const int64_t *strides, int B, int N,
+                           int d, int dtype, float scale, void *stream);
+
+/* ---- fused score-then-select top-k attention ----------------------------- */
+/* Scores every peer, keeps `topk` of them under `mode`, softmax over the
+ * retained scores, V gather-aggregate; writes only `out` (and `idx_out`).
+ * topk must lie in [1, N-1] (the Python layer clamps as the reference does).
+ * idx_out: optional int32 [B, N, topk] contiguous, the retained peers in rank
+ * order (score descending, ties by the mode's rule); supported for the ARGMAX
+ * and SORT modes with topk <= 8, otherwise TARMAC_ERR_MODE.
+ * ARGMAX / SORT with topk <= 8 stream the keys (any N); THRESHOLD mode and
+ * topk > 8 use the resident-row path, N <= 1024 (TARMAC_ERR_N_TOO_LARGE).
+ * Replaces fused_topk_attention, fused_topk_attention_tiled,
+ * fused_topk_attention_masked and fused_topk_attention_sort
+ * (src/kernels/fused_topk_attention.py:56-110, 127-208, 211-289, 296-387,
+ * 405-540). */
+int tarmac_topk_attention(const void *q, const void *k, const void *v,
+                          void *out, const int64_t *strides, int B, int N,
+                          int d, int dtype, float scale, int topk, int mode,
+                          int32_t *idx_out, void *stream);
+
+/* ---- streaming top-k attention ------------------------------------------- */
+/* Exact top-k with keys streamed through shared memory: no N cap, topk <= 8,
+ * lowest index wins a tie. idx_out optional int32 [B, N, topk] contiguous, in
+ * rank order. Replaces streaming_topk_attention and _streaming_topk_kernel
+ * (src/kernels/streaming_topk_attention.py:66-179, 206-258). */
+int tarmac_streaming_topk_attention(const void *q, const void *k,
+                                    const void *v, void *out,
+                                    const int64_t *strides, int B, int N,
+                                    int d, int dtype, float scale, int topk,
+                                    int32_t *idx_out, void *stream);
+
+/* ---- attention over a given peer set (select-before-scoring) ------------- */
+/* idx: [B, N, kk] contiguous peer indices, int64 when idx_is_i64 else int32.
+ * Online softmax over the kk given peers in order; no gathered tensor. A row
+ * naming an index outside [0, N) is written as NaN (no out-of-bounds read).
+ * Replaces fused_prescore_attention and _fused_prescore_kernel
+ * (src/kernels/fused_prescore_attention.py:27-114) and the eager
+ * prescore_attention (src/kernels/prescore_selection.py:442-453). */
+int tarmac_prescore_attention(const void *q, const void *k, const void *v,
+                              void *out, const int64_t *strides,
+                              const void *idx, int idx_is_i64, int kk, int B,
+                              int N, int d, int dtype, float scale,
+                              void *stream);
+
+/* ---- Morton (Z-order) selector ------------------------------------------- */
+/* pos: fp32 [B, N, 2] contiguous positions. Per episode: min/max normalise,
+ * quantise to `bits` per axis (truncation, clamp), interleave x bits at even
+ * and y bits at odd positions. code_out: int64 [B, N].
+ * Replaces _morton_code (src/kernels/prescore_selection.py:313-326). */
+int tarmac_morton_code(const float *pos, int B, int N, int bits,
+                       int64_t *code_out, void *stream);
+
+/* Codes as above, stable ascending sort per episode (ties by agent index),
+ * then for agent at rank r the peers at ranks r+1..r+h and r-1..r-(k-h)
+ * modulo N, h = (k+1)/2. idx_out: int64 [B, N, k]. N <= 4096, 1 <= k <= N-1.
+ * Replaces select_morton_window (src/kernels/prescore_selection.py:329-342),
+ * with the bit width as a parameter (the reference fixes 10). */
+int tarmac_morton_select(const float *pos, int B, int N, int k, int bits,
+                         int64_t *idx_out, void *stream);
+
+/* Fused select-before-scoring: Morton window selection as in
+ * tarmac_morton_select followed by attention over the selected peers as in
+ * tarmac_prescore_attention, one kernel, no index tensor written unless
+ * idx_out (int64 [B, N, k], optional) is given. N <= 4096.
+ * Replaces prescore_full(q, k, v, pos, kk, "morton_window")
+ * (src/kernels/prescore_selection.py:456-458). */
+int tarmac_morton_prescore_attention(const void *q, const void *k,
+                                     const void *v, void *out,
+                                     const int64_t *strides, const float *pos,
+                                     int B, int N, int d, int dtype,
+                                     float scale, int topk, int bits,
+                                     int64_t *idx_out, void *stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TARMAC_B200_H */

@@ -1,0 +1,292 @@
+"""numpy restatement of the reference's attention-core algorithm.
+
+TEST INFRASTRUCTURE ONLY (see oracle/__init__.py): imported by tests/,
+__graft_entry__.smoke() and bench.py's CPU legs, never by the product path.
+
+Every function names the reference lines it restates (paths are within the
+MHHamdan/TopK-TarMAC project). Inputs are numpy arrays: q, k, v float32
+[B, N, d] (bf16 inputs are passed as the float32 values of the same rounded
+numbers), pos float32 [B, N, 2]. Work is done ``CHUNK`` episodes at a time so
+large batches stay within host memory.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+CHUNK = 64
+U32 = 2.0 ** -24  # unit roundoff of fp32
+
+
+def _bmm(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Batched a @ b as one BLAS product per episode (numpy's stacked matmul
+    is several times slower than a loop of 2-D products here)."""
+    out = np.empty(a.shape[:-1] + b.shape[-1:], dtype=np.result_type(a, b))
+    for i in range(a.shape[0]):
+        np.matmul(a[i], b[i], out=out[i])
+    return out
+
+
+def _chunks(B: int):
+    for b0 in range(0, B, CHUNK):
+        yield slice(b0, min(B, b0 + CHUNK))
+
+
+def scores_f64(q: np.ndarray, k: np.ndarray, d_scale: float | None = None):
+    """Exact-as-possible scaled scores in float64 with the diagonal at -inf.
+
+    fused_topk_attention.py:395-397: ``q @ k^T / sqrt(d)``, diagonal masked.
+    Products of fp32 values are exact in float64, so this is the true score to
+    about 1e-16 relative.
+    """
+    d = q.shape[-1]
+    sc = (1.0 / np.sqrt(d)) if d_scale is None else d_scale
+    s = _bmm(q.astype(np.float64), np.swapaxes(k.astype(np.float64), -1, -2))
+    s *= sc
+    N = q.shape[1]
+    s[:, np.arange(N), np.arange(N)] = -np.inf
+    return s
+
+
+def scores_f32(q: np.ndarray, k: np.ndarray):
+    """fp32 scores as the reference forms them: the dot product rounded to
+    fp32, then divided by fp32(sqrt(d)) (fused_topk_attention.py:395), with the
+    diagonal at -inf (fused_topk_attention.py:396-397).
+
+    The dot product is evaluated in float64 and rounded once, so it does not
+    depend on a BLAS summation order.
+    """
+    d = q.shape[-1]
+    dot = _bmm(q.astype(np.float64),
+               np.swapaxes(k.astype(np.float64), -1, -2)).astype(np.float32)
+    s = dot / np.float32(np.sqrt(d))
+    N = q.shape[1]
+    s[:, np.arange(N), np.arange(N)] = -np.inf
+    return s
+
+
+def select_mask(s: np.ndarray, topk: int, tie: str = "low") -> np.ndarray:
+    """Boolean [.., N] mask of the retained peers of each score row.
+
+    Retained = every score above the k-th largest value T, plus the peers
+    tied at T chosen by ``tie``:
+      "low"  — the lowest indices (k argmax rounds, fused_topk_attention.py:
+               275-284; packed (ordkey<<32)|(0x7FFFFFFF-idx) words,
+               streaming_topk_attention.py:114-117);
+      "high" — the highest indices (descending sort of (key<<32)|idx,
+               fused_topk_attention.py:469-479);
+      "all"  — all of them (bisection threshold keeps keys >= T,
+               fused_topk_attention.py:180-191).
+    Exactly k peers are kept for "low"/"high"; "all" keeps k or more.
+    """
+    if tie not in ("low", "high", "all"):
+        raise ValueError(f"unknown tie rule {tie!r}")
+    N = s.shape[-1]
+    T = np.partition(s, N - topk, axis=-1)[..., N - topk]
+    ge = s >= T[..., None]
+    if tie == "all":
+        return ge
+    # rows with more than k peers >= T have surplus ties at T: rank the tied
+    # peers by index and keep the first (low) or last (high) ones needed
+    extra = ge.sum(-1) > topk
+    if extra.any():
+        rows = np.nonzero(extra)
+        sr, Tr = s[rows], T[rows][:, None]
+        eq = sr == Tr
+        need = topk - (sr > Tr).sum(-1)
+        if tie == "low":
+            rank = np.cumsum(eq, axis=-1)
+        else:
+            rank = np.cumsum(eq[:, ::-1], axis=-1)[:, ::-1]
+        ge[rows] = (sr > Tr) | (eq & (rank <= need[:, None]))
+    return ge
+
+
+def topk_indices(s: np.ndarray, topk: int, tie: str = "low") -> np.ndarray:
+    """Retained peers, int64 [.., topk], in rank order: score descending,
+    ties by index ascending ("low") or descending ("high")."""
+    mask = select_mask(s, topk, tie)
+    shp = s.shape[:-1]
+    flat_s = s.reshape(-1, s.shape[-1])
+    flat_m = mask.reshape(-1, s.shape[-1])
+    out = np.empty((flat_s.shape[0], topk), dtype=np.int64)
+    cols = np.nonzero(flat_m)[1].reshape(-1, topk)  # index-ascending per row
+    if tie == "high":
+        cols = cols[:, ::-1]
+    vals = np.take_along_axis(flat_s, cols, axis=1)
+    order = np.argsort(-vals, axis=1, kind="stable")
+    out[:] = np.take_along_axis(cols, order, axis=1)
+    return out.reshape(*shp, topk)
+
+
+def topk_attention(q, k, v, topk: int, tie: str = "low", exact: bool = True,
+                   want_mask: bool = True):
+    """Fused score-then-select top-k attention.
+
+    fused_topk_attention.py:390-402 (reference_topk_attention): scores, mask
+    the diagonal, keep k peers, softmax over the retained scores, weighted sum
+    of the retained V rows. ``topk`` is clamped to [1, N-1] as the reference's
+    launchers do (fused_topk_attention.py:310).
+
+    exact=True (the checker): the selection runs on correctly rounded fp32
+    scores (scores_f32) and the softmax and sum in float64.
+    exact=False (the timed CPU baseline): every step in fp32 as the
+    reference's eager path computes it (fp32 BLAS product, fp32 softmax).
+
+    Returns (out float32 [B, N, d], mask bool [B, N, N] or None).
+    """
+    B, N, d = q.shape
+    topk = max(1, min(topk, N - 1))
+    out = np.empty((B, N, d), dtype=np.float32)
+    masks = np.empty((B, N, N), dtype=bool) if want_mask else None
+    diag = np.arange(N)
+    for sl in _chunks(B):
+        if exact:
+            s = scores_f32(q[sl], k[sl])
+        else:
+            s = _bmm(q[sl], np.swapaxes(k[sl], -1, -2)) / np.float32(np.sqrt(d))
+            s[:, diag, diag] = -np.inf
+        m = select_mask(s, topk, tie)
+        if exact:
+            s64 = np.where(m, s.astype(np.float64), -np.inf)
+            mx = s64.max(-1, keepdims=True)
+            e = np.exp(s64 - mx)
+            w = e / e.sum(-1, keepdims=True)
+            out[sl] = _bmm(w, v[sl].astype(np.float64)).astype(np.float32)
+        elif tie == "all":
+            s32 = np.where(m, s, np.float32(-np.inf))
+            e = np.exp(s32 - s32.max(-1, keepdims=True))
+            w = e / e.sum(-1, keepdims=True)
+            out[sl] = _bmm(w, v[sl])
+        else:
+            # gathered form (mappo.py:217-223): k scores, k-wide softmax,
+            # gather the k value rows, k-term weighted sum
+            nb = s.shape[0]
+            ind = np.nonzero(m.reshape(-1, N))[1].reshape(nb, N, topk)
+            val = np.take_along_axis(s, ind, -1)
+            e = np.exp(val - val.max(-1, keepdims=True))
+            w = e / e.sum(-1, keepdims=True)
+            vg = v[sl][np.arange(nb)[:, None, None], ind]      # [b, N, k, d]
+            out[sl] = np.einsum("bnk,bnkd->bnd", w, vg)
+        if want_mask:
+            masks[sl] = m
+    return out, masks
+
+
+def dense_attention(q, k, v):
+    """softmax(q k^T / sqrt(d), diagonal masked) v, float64 arithmetic.
+
+    dense_unfused (scripts/bench_attention_core.py:69-75) and
+    _flash_dense_kernel (src/kernels/fused_dense_attention.py:38-99).
+    """
+    B, N, d = q.shape
+    out = np.empty((B, N, d), dtype=np.float32)
+    for sl in _chunks(B):
+        s = scores_f64(q[sl], k[sl])
+        mx = s.max(-1, keepdims=True)
+        e = np.exp(s - mx)
+        w = e / e.sum(-1, keepdims=True)
+        out[sl] = _bmm(w, v[sl].astype(np.float64)).astype(np.float32)
+    return out
+
+
+def prescore_attention(q, k, v, idx):
+    """Attention over the given peers idx [B, N, kk].
+
+    prescore_attention (src/kernels/prescore_selection.py:442-453): gather the
+    kk key and value rows, scores q.k_j / sqrt(d), softmax over the kk, sum.
+    float64 arithmetic. Rows naming a peer outside [0, N) are NaN.
+    """
+    B, N, d = q.shape
+    idx = np.asarray(idx, dtype=np.int64)
+    bad = ((idx < 0) | (idx >= N)).any(-1)
+    safe = np.clip(idx, 0, N - 1)
+    bi = np.arange(B)[:, None, None]
+    kg = k.astype(np.float64)[bi, safe]            # [B, N, kk, d]
+    vg = v.astype(np.float64)[bi, safe]
+    s = np.einsum("bnd,bnjd->bnj", q.astype(np.float64), kg) / np.sqrt(d)
+    mx = s.max(-1, keepdims=True)
+    e = np.exp(s - mx)
+    w = e / e.sum(-1, keepdims=True)
+    out = np.einsum("bnj,bnjd->bnd", w, vg).astype(np.float32)
+    out[bad] = np.nan
+    return out
+
+
+_SPREAD = ((8, 0x00FF00FF), (4, 0x0F0F0F0F), (2, 0x33333333), (1, 0x55555555))
+
+
+def _spread_bits(x: np.ndarray) -> np.ndarray:
+    """Insert a zero between consecutive bits of a value below 2^16
+    (prescore_selection.py:313-317; its first (16, 0x0000FFFF) step is the
+    identity for such values)."""
+    x = x.astype(np.int64)
+    for sh, mask in _SPREAD:
+        x = (x | (x << sh)) & mask
+    return x
+
+
+def morton_code(pos: np.ndarray, bits: int = 10) -> np.ndarray:
+    """int64 [B, N] Morton codes (prescore_selection.py:320-326).
+
+    Per episode and axis: lo/hi = min/max, span = max(hi - lo, 1e-6),
+    g = trunc((pos - lo) / span * (2^bits - 1)) clamped to [0, 2^bits - 1],
+    code = spread(gx) | spread(gy) << 1. Every step is a single rounded fp32
+    operation, as the reference's elementwise tensor ops are.
+    """
+    pos = np.asarray(pos, dtype=np.float32)
+    lo = pos.min(axis=1, keepdims=True)
+    hi = pos.max(axis=1, keepdims=True)
+    span = np.maximum(hi - lo, np.float32(1e-6))
+    g = ((pos - lo) / span) * np.float32(2 ** bits - 1)
+    gi = np.clip(np.trunc(g).astype(np.int64), 0, 2 ** bits - 1)
+    return _spread_bits(gi[..., 0]) | (_spread_bits(gi[..., 1]) << 1)
+
+
+def morton_window(pos: np.ndarray, k: int, bits: int = 10) -> np.ndarray:
+    """int64 [B, N, k] Z-order window peers (prescore_selection.py:329-342).
+
+    Agents sorted by code (stable: equal codes keep index order); the agent at
+    rank r keeps the agents at ranks r+1..r+h and r-1..r-(k-h), modulo N,
+    h = (k+1)//2, in that order. The reference sorts with an unstable argsort
+    (line 333); the stable order is the deterministic member of its outcomes.
+    """
+    code = morton_code(pos, bits)
+    B, N = code.shape
+    order = np.argsort(code, axis=-1, kind="stable")
+    rank = np.empty_like(order)
+    np.put_along_axis(rank, order, np.broadcast_to(np.arange(N), (B, N)), -1)
+    half = (k + 1) // 2
+    offs = np.array(list(range(1, half + 1)) + [-o for o in range(1, k - half + 1)],
+                    dtype=np.int64)
+    nr = (rank[..., None] + offs) % N
+    return np.take_along_axis(order, nr.reshape(B, N * k), -1).reshape(B, N, k)
+
+
+def ambiguous_rows(q, k, topk: int, ulps: float = 2.0) -> np.ndarray:
+    """Rows whose retained set is not determined by fp32 arithmetic.
+
+    A row is ambiguous when its k-th and (k+1)-th exact scores differ, but by
+    no more than the error bound of an fp32 dot product of length d
+    (``ulps * (d + 2) * u * sum_c |q_c k_c| * scale`` for either candidate,
+    u = 2^-24): two correct fp32 evaluations of the scores may then order the
+    pair differently. Exact ties (difference 0) are not ambiguous: the tie rule
+    decides them. The reference counts such rows instead of failing on them
+    (scripts/bench_attention_core.py:386-395).
+    """
+    B, N, d = q.shape
+    topk = max(1, min(topk, N - 1))
+    if topk >= N - 1:
+        return np.zeros((B, N), dtype=bool)
+    res = np.empty((B, N), dtype=bool)
+    sc = 1.0 / np.sqrt(d)
+    for sl in _chunks(B):
+        s = scores_f64(q[sl], k[sl])
+        mag = _bmm(np.abs(q[sl].astype(np.float64)),
+                        np.swapaxes(np.abs(k[sl].astype(np.float64)), -1, -2)) * sc
+        srt = np.sort(s, axis=-1)[..., ::-1]
+        a, b = srt[..., topk - 1], srt[..., topk]
+        tol = ulps * (d + 2) * U32 * mag.max(-1)
+        gap = a - b
+        res[sl] = (gap > 0) & (gap <= tol)
+    return res

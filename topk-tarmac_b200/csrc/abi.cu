@@ -1,0 +1,227 @@
+// abi.cu — the extern "C" entry points declared in include/tarmac_b200.h.
+//
+// Each entry point validates its arguments, fills an AttnParams, picks the
+// kernel for the (mode, k, N, d, dtype) combination and launches it on the
+// caller's stream. No memory is allocated and no stream is synchronised.
+#include <math.h>
+
+#include "common.cuh"
+
+namespace tarmac {
+cudaError_t launch_topk_stream_f32(const AttnParams& p, bool tie_high,
+                                   cudaStream_t s);
+cudaError_t launch_topk_stream_bf16(const AttnParams& p, bool tie_high,
+                                    cudaStream_t s);
+static cudaError_t launch_topk_stream(const AttnParams& p, int dtype,
+                                      bool tie_high, cudaStream_t s) {
+  return dtype == TARMAC_BF16 ? launch_topk_stream_bf16(p, tie_high, s)
+                              : launch_topk_stream_f32(p, tie_high, s);
+}
+cudaError_t launch_topk_rows(const AttnParams& p, int dtype, cudaStream_t s);
+cudaError_t launch_dense(const AttnParams& p, int dtype, cudaStream_t s);
+cudaError_t launch_prescore(const AttnParams& p, int dtype, const void* idx,
+                            bool idx_i64, int kk, cudaStream_t s);
+cudaError_t launch_morton_code(const float* pos, int B, int N, int bits,
+                               int64_t* out, cudaStream_t s);
+cudaError_t launch_morton_select(const float* pos, int B, int N, int k,
+                                 int bits, int64_t* idx_out, cudaStream_t s);
+cudaError_t launch_morton_prescore(const AttnParams& p, int dtype,
+                                   const float* pos, int bits,
+                                   int64_t* idx_out, cudaStream_t s);
+
+constexpr int MAX_D = 128;
+constexpr int RESIDENT_MAX_N = 1024;
+constexpr int STREAM_MAX_K = 8;
+constexpr int REGISTER_MAX_K = 8;
+constexpr int MORTON_MAX_N = 4096;
+
+static bool aligned(const void* ptr, uintptr_t a) {
+  return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0;
+}
+
+static int elem_size(int dtype) { return dtype == TARMAC_BF16 ? 2 : 4; }
+
+// Validate the operand block and fill p. Returns TARMAC_OK or an error code.
+static int fill_params(AttnParams& p, const void* q, const void* k,
+                       const void* v, void* out, const int64_t* strides, int B,
+                       int N, int d, int dtype, float scale) {
+  if (!q || !k || !v || !out) return TARMAC_ERR_NULL;
+  if (dtype != TARMAC_F32 && dtype != TARMAC_BF16) return TARMAC_ERR_DTYPE;
+  if (B < 0 || N < 2 || d < 1 || d > MAX_D) return TARMAC_ERR_SHAPE;
+  const int es = elem_size(dtype);
+  if (!aligned(q, es) || !aligned(k, es) || !aligned(v, es) || !aligned(out, es))
+    return TARMAC_ERR_ALIGN;
+  Strides st;
+  if (strides) {
+    st = Strides{strides[0], strides[1], strides[2], strides[3],
+                 strides[4], strides[5], strides[6], strides[7]};
+  } else {
+    const int64_t rs = d, bs = (int64_t)N * d;
+    st = Strides{bs, rs, bs, rs, bs, rs, bs, rs};
+  }
+  // Vector path: 4-element groups, 16-byte (fp32) / 8-byte (bf16) aligned.
+  const uintptr_t va = (uintptr_t)(4 * es);
+  bool vec = (d % 4) == 0 && aligned(q, va) && aligned(k, va) &&
+             aligned(v, va) && aligned(out, va);
+  const int64_t sv[8] = {st.qb, st.qn, st.kb, st.kn, st.vb, st.vn, st.ob, st.on};
+  for (int i = 0; i < 8; ++i) vec = vec && (sv[i] % 4) == 0;
+  p.q = q; p.k = k; p.v = v; p.o = out;
+  p.st = st;
+  p.B = B; p.N = N; p.d = d;
+  p.topk = 0;
+  p.mode = TARMAC_SELECT_ARGMAX;
+  // A power-of-two scale is folded into q exactly; any other scale is applied
+  // to the scores after the dot product, as the reference applies it.
+  int ex = 0;
+  const float mant = frexpf(scale, &ex);
+  const bool pow2 = scale > 0.f && mant == 0.5f && ex > -100 && ex < 100;
+  p.qscale = pow2 ? scale : 1.0f;
+  p.post_scale = pow2 ? 1.0f : scale;
+  p.idx_out = nullptr;
+  p.vec = vec ? 1 : 0;
+  return TARMAC_OK;
+}
+
+static int launch_status(cudaError_t e) {
+  return e == cudaSuccess ? TARMAC_OK : TARMAC_ERR_LAUNCH;
+}
+
+}  // namespace tarmac
+
+using namespace tarmac;
+
+extern "C" {
+
+int tarmac_abi_version(void) { return TARMAC_ABI_VERSION; }
+
+const char* tarmac_strerror(int status) {
+  switch (status) {
+    case TARMAC_OK: return "ok";
+    case TARMAC_ERR_NULL: return "a required pointer is NULL";
+    case TARMAC_ERR_SHAPE: return "B, N or d outside the supported range (N >= 2, 1 <= d <= 128)";
+    case TARMAC_ERR_DTYPE: return "dtype must be TARMAC_F32 or TARMAC_BF16";
+    case TARMAC_ERR_TOPK: return "k outside [1, N-1] or above this path's limit";
+    case TARMAC_ERR_N_TOO_LARGE: return "N above this path's limit";
+    case TARMAC_ERR_ALIGN: return "pointer not aligned to its element size";
+    case TARMAC_ERR_MODE: return "unknown selection mode or unsupported combination";
+    case TARMAC_ERR_LAUNCH: return "CUDA kernel launch failed";
+    case TARMAC_ERR_BITS: return "Morton bits must lie in [1, 16]";
+    default: return "unknown status";
+  }
+}
+
+int tarmac_dense_attention(const void* q, const void* k, const void* v,
+                           void* out, const int64_t* strides, int B, int N,
+                           int d, int dtype, float scale, void* stream) {
+  AttnParams p;
+  int st = fill_params(p, q, k, v, out, strides, B, N, d, dtype, scale);
+  if (st != TARMAC_OK) return st;
+  if (B == 0) return TARMAC_OK;
+  return launch_status(launch_dense(p, dtype, (cudaStream_t)stream));
+}
+
+int tarmac_topk_attention(const void* q, const void* k, const void* v,
+                          void* out, const int64_t* strides, int B, int N,
+                          int d, int dtype, float scale, int topk, int mode,
+                          int32_t* idx_out, void* stream) {
+  AttnParams p;
+  int st = fill_params(p, q, k, v, out, strides, B, N, d, dtype, scale);
+  if (st != TARMAC_OK) return st;
+  if (mode != TARMAC_SELECT_ARGMAX && mode != TARMAC_SELECT_THRESHOLD &&
+      mode != TARMAC_SELECT_SORT)
+    return TARMAC_ERR_MODE;
+  if (topk < 1 || topk > N - 1) return TARMAC_ERR_TOPK;
+  p.topk = topk;
+  p.mode = mode;
+  const bool reg = mode != TARMAC_SELECT_THRESHOLD && topk <= REGISTER_MAX_K;
+  if (idx_out && !reg) return TARMAC_ERR_MODE;
+  if (!reg && N > RESIDENT_MAX_N) return TARMAC_ERR_N_TOO_LARGE;
+  if (idx_out && !aligned(idx_out, 4)) return TARMAC_ERR_ALIGN;
+  p.idx_out = idx_out;
+  if (B == 0) return TARMAC_OK;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (reg)
+    return launch_status(
+        launch_topk_stream(p, dtype, mode == TARMAC_SELECT_SORT, s));
+  return launch_status(launch_topk_rows(p, dtype, s));
+}
+
+int tarmac_streaming_topk_attention(const void* q, const void* k,
+                                    const void* v, void* out,
+                                    const int64_t* strides, int B, int N,
+                                    int d, int dtype, float scale, int topk,
+                                    int32_t* idx_out, void* stream) {
+  AttnParams p;
+  int st = fill_params(p, q, k, v, out, strides, B, N, d, dtype, scale);
+  if (st != TARMAC_OK) return st;
+  if (topk < 1 || topk > N - 1 || topk > STREAM_MAX_K) return TARMAC_ERR_TOPK;
+  if (idx_out && !aligned(idx_out, 4)) return TARMAC_ERR_ALIGN;
+  p.topk = topk;
+  p.idx_out = idx_out;
+  if (B == 0) return TARMAC_OK;
+  return launch_status(
+      launch_topk_stream(p, dtype, false, (cudaStream_t)stream));
+}
+
+int tarmac_prescore_attention(const void* q, const void* k, const void* v,
+                              void* out, const int64_t* strides,
+                              const void* idx, int idx_is_i64, int kk, int B,
+                              int N, int d, int dtype, float scale,
+                              void* stream) {
+  AttnParams p;
+  int st = fill_params(p, q, k, v, out, strides, B, N, d, dtype, scale);
+  if (st != TARMAC_OK) return st;
+  if (!idx) return TARMAC_ERR_NULL;
+  if (kk < 1) return TARMAC_ERR_TOPK;
+  if (!aligned(idx, idx_is_i64 ? 8 : 4)) return TARMAC_ERR_ALIGN;
+  if (B == 0) return TARMAC_OK;
+  return launch_status(launch_prescore(p, dtype, idx, idx_is_i64 != 0, kk,
+                                       (cudaStream_t)stream));
+}
+
+int tarmac_morton_code(const float* pos, int B, int N, int bits,
+                       int64_t* code_out, void* stream) {
+  if (!pos || !code_out) return TARMAC_ERR_NULL;
+  if (B < 0 || N < 1) return TARMAC_ERR_SHAPE;
+  if (bits < 1 || bits > 16) return TARMAC_ERR_BITS;
+  if (!aligned(pos, 8) || !aligned(code_out, 8)) return TARMAC_ERR_ALIGN;
+  if (B == 0) return TARMAC_OK;
+  return launch_status(
+      launch_morton_code(pos, B, N, bits, code_out, (cudaStream_t)stream));
+}
+
+int tarmac_morton_select(const float* pos, int B, int N, int k, int bits,
+                         int64_t* idx_out, void* stream) {
+  if (!pos || !idx_out) return TARMAC_ERR_NULL;
+  if (B < 0 || N < 2) return TARMAC_ERR_SHAPE;
+  if (N > MORTON_MAX_N) return TARMAC_ERR_N_TOO_LARGE;
+  if (k < 1 || k > N - 1) return TARMAC_ERR_TOPK;
+  if (bits < 1 || bits > 16) return TARMAC_ERR_BITS;
+  if (!aligned(pos, 8) || !aligned(idx_out, 8)) return TARMAC_ERR_ALIGN;
+  if (B == 0) return TARMAC_OK;
+  return launch_status(
+      launch_morton_select(pos, B, N, k, bits, idx_out, (cudaStream_t)stream));
+}
+
+int tarmac_morton_prescore_attention(const void* q, const void* k,
+                                     const void* v, void* out,
+                                     const int64_t* strides, const float* pos,
+                                     int B, int N, int d, int dtype,
+                                     float scale, int topk, int bits,
+                                     int64_t* idx_out, void* stream) {
+  AttnParams p;
+  int st = fill_params(p, q, k, v, out, strides, B, N, d, dtype, scale);
+  if (st != TARMAC_OK) return st;
+  if (!pos) return TARMAC_ERR_NULL;
+  if (N > MORTON_MAX_N) return TARMAC_ERR_N_TOO_LARGE;
+  if (topk < 1 || topk > N - 1) return TARMAC_ERR_TOPK;
+  if (bits < 1 || bits > 16) return TARMAC_ERR_BITS;
+  if (!aligned(pos, 8)) return TARMAC_ERR_ALIGN;
+  if (idx_out && !aligned(idx_out, 8)) return TARMAC_ERR_ALIGN;
+  p.topk = topk;
+  if (B == 0) return TARMAC_OK;
+  return launch_status(launch_morton_prescore(p, dtype, pos, bits, idx_out,
+                                              (cudaStream_t)stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,170 @@
+// common.cuh — device helpers shared by the TarMAC attention-core kernels.
+//
+// Layout convention (see include/tarmac_b200.h): Q, K, V, O are [B, N, d]
+// arrays of fp32 or bf16 with unit innermost stride; batch and row strides are
+// given in elements. Inside the kernels every row is widened to fp32 and padded
+// with zeros to DP (a power of two >= d), so all arithmetic is fp32.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/tarmac_b200.h"
+
+namespace tarmac {
+
+// Element strides (in elements) of the four [B, N, d] operands.
+struct Strides {
+  int64_t qb, qn, kb, kn, vb, vn, ob, on;
+};
+
+// Everything an attention kernel needs; passed by value (kernel parameter).
+struct AttnParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  Strides st;
+  int B, N, d;
+  int topk;            // retained peers (top-k kernels)
+  int mode;            // TARMAC_SELECT_* (resident-row kernel)
+  float qscale;        // folded into q at load time (exact: a power of two)
+  float post_scale;    // applied to the retained scores (1 when folded)
+  int32_t* idx_out;    // optional [B, N, topk] rank-ordered retained peers
+  int vec;             // 1: rows may be moved with 16-byte vector accesses
+};
+
+__host__ __device__ constexpr int cdiv(int a, int b) { return (a + b - 1) / b; }
+
+// ---------------------------------------------------------------------------
+// element conversion
+// ---------------------------------------------------------------------------
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+// Load 4 consecutive elements starting at p (p is 16-byte aligned for fp32,
+// 8-byte aligned for bf16 when `vec` holds) into fp32.
+__device__ __forceinline__ float4 load4(const float* p) {
+  return __ldg(reinterpret_cast<const float4*>(p));
+}
+__device__ __forceinline__ float4 load4(const __nv_bfloat16* p) {
+  uint2 u = __ldg(reinterpret_cast<const uint2*>(p));
+  __nv_bfloat162 lo = *reinterpret_cast<__nv_bfloat162*>(&u.x);
+  __nv_bfloat162 hi = *reinterpret_cast<__nv_bfloat162*>(&u.y);
+  float2 a = __bfloat1622float2(lo);
+  float2 b = __bfloat1622float2(hi);
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
+// Load the first `d` elements of a row into x[0..DP), zero beyond d.
+// vec: d is a multiple of 4 (fp32) / 8 (bf16) and the row is 16-byte aligned.
+template <int DP, typename T>
+__device__ __forceinline__ void load_row(float (&x)[DP], const T* p, int d,
+                                         bool vec) {
+  if (vec) {
+#pragma unroll
+    for (int c = 0; c < DP; c += 4) {
+      if (c < d) {
+        float4 f = load4(p + c);
+        x[c] = f.x; x[c + 1] = f.y; x[c + 2] = f.z; x[c + 3] = f.w;
+      } else {
+        x[c] = 0.f; x[c + 1] = 0.f; x[c + 2] = 0.f; x[c + 3] = 0.f;
+      }
+    }
+  } else {
+#pragma unroll
+    for (int c = 0; c < DP; ++c) x[c] = (c < d) ? to_f32<T>(p[c]) : 0.f;
+  }
+}
+
+// Store the first `d` values of x to a row.
+template <int DP, typename T>
+__device__ __forceinline__ void store_row(T* p, const float (&x)[DP], int d,
+                                          bool vec) {
+  if constexpr (sizeof(T) == 4) {
+    if (vec) {
+#pragma unroll
+      for (int c = 0; c < DP; c += 4)
+        if (c < d)
+          *reinterpret_cast<float4*>(p + c) =
+              make_float4(x[c], x[c + 1], x[c + 2], x[c + 3]);
+      return;
+    }
+  } else {
+    if (vec) {
+#pragma unroll
+      for (int c = 0; c < DP; c += 4)
+        if (c < d) {
+          __nv_bfloat162 lo = __floats2bfloat162_rn(x[c], x[c + 1]);
+          __nv_bfloat162 hi = __floats2bfloat162_rn(x[c + 2], x[c + 3]);
+          uint2 u;
+          u.x = *reinterpret_cast<uint32_t*>(&lo);
+          u.y = *reinterpret_cast<uint32_t*>(&hi);
+          *reinterpret_cast<uint2*>(p + c) = u;
+        }
+      return;
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < DP; ++c)
+    if (c < d) p[c] = from_f32<T>(x[c]);
+}
+
+// Monotone map fp32 -> uint32: a < b (as non-NaN floats) iff key(a) < key(b).
+// Restates _float_to_ordered_int (fused_topk_attention.py:113-124) in unsigned
+// form (offset by 2^31, so the order is the same).
+__device__ __forceinline__ uint32_t ordered_key(float x) {
+  uint32_t u = __float_as_uint(x);
+  return u ^ ((u & 0x80000000u) ? 0xFFFFFFFFu : 0x80000000u);
+}
+__device__ __forceinline__ float key_to_float(uint32_t k) {
+  uint32_t u = (k & 0x80000000u) ? (k ^ 0x80000000u) : ~k;
+  return __uint_as_float(u);
+}
+
+// Stage rows [r0, r0 + nrows) of a [N, d] episode (row stride `rs`) into a
+// shared fp32 tile [TK][DP], zero-padding rows >= N and columns >= d.
+// All threads of the block participate.
+template <int DP, int TK, typename T>
+__device__ __forceinline__ void stage_tile(float* __restrict__ tile,
+                                           const T* __restrict__ base,
+                                           int64_t rs, int r0, int N, int d,
+                                           bool vec) {
+  constexpr int C4 = DP / 4;
+  for (int e = threadIdx.x; e < TK * C4; e += blockDim.x) {
+    int row = e / C4;
+    int c = (e - row * C4) * 4;
+    int r = r0 + row;
+    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (r < N && c < d) {
+      const T* p = base + (int64_t)r * rs + c;
+      if (vec) {
+        f = load4(p);
+      } else {
+        f.x = to_f32<T>(p[0]);
+        f.y = (c + 1 < d) ? to_f32<T>(p[1]) : 0.f;
+        f.z = (c + 2 < d) ? to_f32<T>(p[2]) : 0.f;
+        f.w = (c + 3 < d) ? to_f32<T>(p[3]) : 0.f;
+      }
+    }
+    *reinterpret_cast<float4*>(tile + row * DP + c) = f;
+  }
+}
+
+}  // namespace tarmac

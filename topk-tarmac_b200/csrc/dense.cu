@@ -1,0 +1,165 @@
+// dense.cu — dense masked-diagonal attention on sm_100a (fp32 arithmetic).
+//
+// Restates the reference's _flash_dense_kernel
+// (src/kernels/fused_dense_attention.py:38-99): softmax(q k^T * scale) v with
+// the diagonal excluded and no score matrix written. The design differs:
+// one thread owns QPT query rows; K and V tiles are staged through shared
+// memory and read with broadcast loads; the online softmax works in base 2
+// and only moves its reference maximum when a score exceeds it by more than
+// 2^RESCALE_LOG2 (a stale maximum leaves every weight bounded by 2^8, so the
+// normaliser cannot overflow, and the final division makes the result
+// independent of the reference point).
+#include "common.cuh"
+
+namespace tarmac {
+
+constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_LOG2 = 8.0f;
+
+template <int DP>
+__host__ __device__ constexpr int dense_tile_keys() {
+  return 8192 / (DP * 4);  // 8 KB of K plus 8 KB of V per tile
+}
+
+template <int DP, int QPT, typename T>
+__global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
+  constexpr int TK = dense_tile_keys<DP>();
+  __shared__ __align__(16) float sk[TK * DP];
+  __shared__ __align__(16) float sv[TK * DP];
+
+  const int N = p.N, d = p.d;
+  const int groups = cdiv(N, 32 * QPT);
+  const int wpb = blockDim.x >> 5;
+  const int cpe = cdiv(groups, wpb);
+  const int b = blockIdx.x / cpe;
+  const int chunk = blockIdx.x - b * cpe;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = chunk * wpb + warp;
+  const bool vec = p.vec != 0;
+  const bool active = g < groups;
+
+  const T* Q = static_cast<const T*>(p.q) + (int64_t)b * p.st.qb;
+  const T* K = static_cast<const T*>(p.k) + (int64_t)b * p.st.kb;
+  const T* V = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
+  T* O = static_cast<T*>(p.o) + (int64_t)b * p.st.ob;
+
+  // scores enter the exponent as s * scale * log2(e)
+  const float c2 = p.post_scale * LOG2E;
+  int qi[QPT];
+  float q[QPT][DP];
+  float acc[QPT][DP];
+  float m[QPT], l[QPT];
+#pragma unroll
+  for (int r = 0; r < QPT; ++r) {
+    qi[r] = g * 32 * QPT + r * 32 + lane;
+    if (active && qi[r] < N) {
+      load_row<DP, T>(q[r], Q + (int64_t)qi[r] * p.st.qn, d, vec);
+#pragma unroll
+      for (int c = 0; c < DP; ++c) q[r][c] *= p.qscale;
+    } else {
+#pragma unroll
+      for (int c = 0; c < DP; ++c) q[r][c] = 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < DP; ++c) acc[r][c] = 0.f;
+    m[r] = -1e30f;
+    l[r] = 0.f;
+  }
+
+  for (int t0 = 0; t0 < N; t0 += TK) {
+    __syncthreads();
+    stage_tile<DP, TK, T>(sk, K, p.st.kn, t0, N, d, vec);
+    stage_tile<DP, TK, T>(sv, V, p.st.vn, t0, N, d, vec);
+    __syncthreads();
+    if (!active) continue;
+    const int nk = min(TK, N - t0);
+#pragma unroll 2
+    for (int jj = 0; jj < nk; ++jj) {
+      const float* kr = sk + jj * DP;
+      const float* vr = sv + jj * DP;
+      float s[QPT];
+#pragma unroll
+      for (int r = 0; r < QPT; ++r) s[r] = 0.f;
+#pragma unroll
+      for (int c = 0; c < DP; c += 4) {
+        const float4 kv = *reinterpret_cast<const float4*>(kr + c);
+#pragma unroll
+        for (int r = 0; r < QPT; ++r) {
+          s[r] = fmaf(q[r][c], kv.x, s[r]);
+          s[r] = fmaf(q[r][c + 1], kv.y, s[r]);
+          s[r] = fmaf(q[r][c + 2], kv.z, s[r]);
+          s[r] = fmaf(q[r][c + 3], kv.w, s[r]);
+        }
+      }
+      const int j = t0 + jj;
+      float pr[QPT];
+#pragma unroll
+      for (int r = 0; r < QPT; ++r) {
+        const float t = (j == qi[r]) ? -INFINITY : s[r] * c2;
+        if (t > m[r] + RESCALE_LOG2) {
+          const float alpha = exp2f(m[r] - t);
+          l[r] *= alpha;
+#pragma unroll
+          for (int c = 0; c < DP; ++c) acc[r][c] *= alpha;
+          m[r] = t;
+        }
+        pr[r] = exp2f(t - m[r]);
+        l[r] += pr[r];
+      }
+#pragma unroll
+      for (int c = 0; c < DP; c += 4) {
+        const float4 vv = *reinterpret_cast<const float4*>(vr + c);
+#pragma unroll
+        for (int r = 0; r < QPT; ++r) {
+          acc[r][c] = fmaf(pr[r], vv.x, acc[r][c]);
+          acc[r][c + 1] = fmaf(pr[r], vv.y, acc[r][c + 1]);
+          acc[r][c + 2] = fmaf(pr[r], vv.z, acc[r][c + 2]);
+          acc[r][c + 3] = fmaf(pr[r], vv.w, acc[r][c + 3]);
+        }
+      }
+    }
+  }
+  if (!active) return;
+#pragma unroll
+  for (int r = 0; r < QPT; ++r) {
+    if (qi[r] >= N) continue;
+    const float inv = 1.0f / l[r];
+    float o[DP];
+#pragma unroll
+    for (int c = 0; c < DP; ++c) o[c] = acc[r][c] * inv;
+    store_row<DP, T>(O + (int64_t)qi[r] * p.st.on, o, d, vec);
+  }
+}
+
+template <int DP>
+constexpr int dense_qpt() {
+  return DP <= 16 ? 2 : 1;
+}
+
+template <int DP, typename T>
+static cudaError_t launch_dense_dp(const AttnParams& p, cudaStream_t s) {
+  constexpr int QPT = dense_qpt<DP>();
+  const int groups = cdiv(p.N, 32 * QPT);
+  const int wpb = groups < 4 ? groups : 4;
+  const int cpe = cdiv(groups, wpb);
+  const int64_t blocks = (int64_t)p.B * cpe;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  dense_kernel<DP, QPT, T><<<(unsigned)blocks, 32 * wpb, 0, s>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t launch_dense_dt(const AttnParams& p, cudaStream_t s) {
+  if (p.d <= 8) return launch_dense_dp<8, T>(p, s);
+  if (p.d <= 16) return launch_dense_dp<16, T>(p, s);
+  if (p.d <= 32) return launch_dense_dp<32, T>(p, s);
+  if (p.d <= 64) return launch_dense_dp<64, T>(p, s);
+  return launch_dense_dp<128, T>(p, s);
+}
+
+cudaError_t launch_dense(const AttnParams& p, int dtype, cudaStream_t s) {
+  return dtype == TARMAC_BF16 ? launch_dense_dt<__nv_bfloat16>(p, s)
+                              : launch_dense_dt<float>(p, s);
+}
+
+}  // namespace tarmac

@@ -1,0 +1,125 @@
+"""Attention-communication module — drop-in for the attention-core part of the
+reference module ``src/agents/mappo.py`` (MHHamdan/TopK-TarMAC).
+
+``MAPPOConfig`` and ``AttentionComm`` keep the reference's names, fields,
+parameters (``qkv``, ``proj``, ``k_gate`` — so reference state dicts load)
+and forward signature ``forward(x, pos=None) -> (msg, info)``
+(mappo.py:31-86, 138-420). The attention core between the qkv projection and
+``proj(gelu(.))`` runs on the sm_100a kernels of ``tarmac_b200``:
+
+``dense``, ``dense_sdpa``   dense masked-diagonal attention (mappo.py:174-190,
+                            361-373)
+``topk``, ``topk_gather``   fused score-then-select top-k, lowest index on a
+                            tie; the two modes compute the same function
+                            (mappo.py:192-231, 374-382)
+``zorder_k``                fused Z-order selection + attention over the
+                            selected peers, 10-bit codes (mappo.py:265-292)
+
+The q, k, v chunks of the qkv output are passed to the kernels as strided
+views (no copies). The kernels are forward-only, like the reference's Triton
+kernels (scripts/bench_attention_core.py:172-176): a backward pass through the
+attention core raises NotImplementedError. The ``random_k``, ``entmax`` and
+``adaptive_topk`` study arms and the MAPPO actor/critic are outside this build.
+The weight-based diagnostics of ``collect_info`` (attention entropy) need the
+weight matrix, which the fused kernels never form; ``info`` carries
+``effective_k`` where the reference reports it.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+import torch.nn as nn
+import torch.nn.functional as F
+
+from tarmac_b200 import ops
+
+#: Slice of a simple_spread observation holding the agent's own position
+#: (mappo.py:24-28).
+SELF_POS = slice(2, 4)
+MORTON_BITS = 10
+
+
+@dataclass
+class MAPPOConfig:
+    obs_dim: int
+    n_actions: int
+    n_agents: int
+    hidden: int = 64
+    use_orthogonal_init: bool = True
+    use_comm: bool = False
+    msg_dim: int = 16
+    n_heads: int = 1
+    attn_mode: str = "dense"
+    topk: int = 0
+    entmax_alpha: float = 1.5
+
+
+def _ortho_init(layer: nn.Linear, gain: float = float(np.sqrt(2.0))) -> None:
+    nn.init.orthogonal_(layer.weight, gain=gain)
+    nn.init.zeros_(layer.bias)
+
+
+class _ForwardOnly(torch.autograd.Function):
+    """Runs a kernel launcher; its backward is not implemented."""
+
+    @staticmethod
+    def forward(ctx, fn, q, k, v, *extra):
+        return fn(q, k, v, *extra)
+
+    @staticmethod
+    def backward(ctx, *grads):
+        raise NotImplementedError(
+            "the tarmac_b200 attention-core kernels are forward-only")
+
+
+class AttentionComm(nn.Module):
+    """Inter-agent attention communication block: (B, N, D_in) -> (B, N, msg_dim)."""
+
+    _MODES = ("dense", "dense_sdpa", "topk", "topk_gather", "zorder_k")
+
+    def __init__(self, cfg: MAPPOConfig, in_dim: int) -> None:
+        super().__init__()
+        self.cfg = cfg
+        self.collect_info = True
+        self.qkv = nn.Linear(in_dim, 3 * cfg.msg_dim)
+        self.proj = nn.Linear(cfg.msg_dim, cfg.msg_dim)
+        self.k_bins = max(cfg.n_agents - 1, 1)
+        self.k_gate = nn.Linear(in_dim, self.k_bins)
+        if cfg.use_orthogonal_init:
+            for layer in (self.qkv, self.proj, self.k_gate):
+                _ortho_init(layer)
+
+    def _k_eff(self, N: int) -> int:
+        return min(max(self.cfg.topk, 1), N - 1)
+
+    def forward(self, x: torch.Tensor,
+                pos: torch.Tensor | None = None) -> tuple[torch.Tensor, dict]:
+        B, N, _ = x.shape
+        mode = self.cfg.attn_mode
+        if mode not in self._MODES:
+            if mode in ("random_k", "entmax", "adaptive_topk"):
+                raise NotImplementedError(
+                    f"attn_mode={mode!r} is outside the tarmac_b200 build")
+            raise ValueError(f"unknown attn_mode {mode!r}")
+        q, k, v = self.qkv(x).chunk(3, dim=-1)
+        info: dict = {}
+        if mode == "zorder_k":
+            if pos is None:
+                raise ValueError("attn_mode='zorder_k' needs agent positions")
+            k_eff = self._k_eff(N)
+            msg = _ForwardOnly.apply(
+                lambda a, b, c, p: ops.morton_prescore_attention(
+                    a, b, c, p, k_eff, MORTON_BITS), q, k, v, pos.float())
+            info["effective_k"] = float(k_eff)
+        elif mode in ("dense", "dense_sdpa"):
+            msg = _ForwardOnly.apply(ops.dense_attention, q, k, v)
+        else:
+            k_eff = self._k_eff(N)
+            msg = _ForwardOnly.apply(
+                lambda a, b, c: ops.topk_attention(a, b, c, k_eff, "argmax"),
+                q, k, v)
+            info["effective_k"] = float(k_eff)
+        return self.proj(F.gelu(msg)), info

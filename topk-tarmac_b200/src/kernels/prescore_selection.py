@@ -1,0 +1,96 @@
+"""Select-before-scoring — drop-in for the reference module
+``src/kernels/prescore_selection.py`` (MHHamdan/TopK-TarMAC).
+
+On the sm_100a kernels of ``tarmac_b200``:
+
+``_morton_code(pos, bits=10)``     per-episode Morton codes (lines 320-326)
+``select_morton_window(pos, k)``   Z-order window peers (lines 329-342); the
+                                   curve order is the stable one (equal codes
+                                   keep agent-index order), the deterministic
+                                   member of the reference's unstable argsort
+``prescore_attention(q,k,v,idx)``  attention over the given peers (442-453)
+``prescore_full(...)``             selector + attention; ``morton_window`` runs
+                                   as one fused kernel (456-458)
+
+Outside this build (importable, raise NotImplementedError): the radius and
+grid kNN selectors (lines 293-300, 345-430) and the selector cost ledger
+``analytic_flops`` (lines 461-470).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from tarmac_b200 import ops
+
+MORTON_BITS = 10  # the reference's _morton_code default
+
+
+def _spread_bits(v: torch.Tensor) -> torch.Tensor:
+    """Insert a zero between consecutive bits of values below 2^16
+    (prescore_selection.py:313-317); elementwise torch on the input's device,
+    kept for callers of the private helper."""
+    for shift, mask in ((8, 0x00FF00FF), (4, 0x0F0F0F0F), (2, 0x33333333),
+                        (1, 0x55555555)):
+        v = (v | (v << shift)) & mask
+    return v
+
+
+def _morton_code(pos: torch.Tensor, bits: int = MORTON_BITS) -> torch.Tensor:
+    """Interleave the bits of quantised 2-D coordinates. pos: (B, N, 2)."""
+    return ops.morton_code(pos, bits)
+
+
+def select_morton_window(pos: torch.Tensor, k: int,
+                         bits: int = MORTON_BITS) -> torch.Tensor:
+    """k peers adjacent along a Z-order curve, int64 (B, N, k)."""
+    return ops.morton_select(pos, k, bits)
+
+
+def _not_built(name: str):
+    raise NotImplementedError(
+        f"{name} is outside the tarmac_b200 build (only the Morton window "
+        "selector is implemented on the GPU)")
+
+
+def select_radius_knn(pos: torch.Tensor, k: int) -> torch.Tensor:
+    _not_built("select_radius_knn")
+
+
+def grid_knn_shape(N: int, k: int) -> tuple[int, int]:
+    """Grid side G and per-cell capacity M (prescore_selection.py:345-359):
+    cells sized for about max(2, k) agents, capacity mean + 3 sd + 2."""
+    occ = max(2, k)
+    G = max(1, int((N / occ) ** 0.5))
+    mean = N / (G * G)
+    return G, int(mean + 3 * mean ** 0.5 + 2)
+
+
+def select_grid_knn(pos: torch.Tensor, k: int) -> torch.Tensor:
+    _not_built("select_grid_knn")
+
+
+def grid_knn_recall(pos: torch.Tensor, k: int) -> float:
+    _not_built("grid_knn_recall")
+
+
+SELECTORS = {"radius_knn": select_radius_knn,
+             "grid_knn": select_grid_knn,
+             "morton_window": select_morton_window}
+
+
+def prescore_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                       idx: torch.Tensor) -> torch.Tensor:
+    """Score only the retained pairs. q,k,v: (B,N,d); idx: (B,N,kk)."""
+    return ops.prescore_attention(q, k, v, idx)
+
+
+def prescore_full(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                  pos: torch.Tensor, kk: int, selector: str) -> torch.Tensor:
+    if selector == "morton_window":
+        return ops.morton_prescore_attention(q, k, v, pos, kk, MORTON_BITS)
+    return prescore_attention(q, k, v, SELECTORS[selector](pos, kk))
+
+
+def analytic_flops(selector: str, B: int, N: int, d: int, kk: int) -> dict:
+    _not_built("analytic_flops (the selector cost ledger)")

@@ -1,0 +1,216 @@
+"""Torch-facing launchers over the C ABI.
+
+Each function takes CUDA tensors, checks them, allocates the output with
+``torch.empty`` (the C ABI itself never allocates) and launches on the current
+stream of the tensors' device. Q, K, V are ``[B, N, d]`` fp32 or bf16 tensors
+with a unit innermost stride; other strides (e.g. the ``qkv.chunk(3, -1)``
+views of the comm module) are passed through without a copy. Nothing here
+computes on the CPU: a CPU tensor or a missing library is an error.
+
+The semantics are those of the reference's eager path
+(src/kernels/fused_topk_attention.py:390-402): scores q.k * scale with the
+diagonal excluded, softmax over the retained peers, weighted sum of V rows.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+_MODES = {"argmax": _lib.SELECT_ARGMAX, "threshold": _lib.SELECT_THRESHOLD,
+          "sort": _lib.SELECT_SORT}
+
+RESIDENT_MAX_N = 1024
+STREAM_MAX_K = 8
+MORTON_MAX_N = 4096
+
+
+def default_scale(d: int) -> float:
+    """1/sqrt(d), as the reference kernels pass it (fused_topk_attention.py:327)."""
+    return 1.0 / (d ** 0.5)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _unit_inner(t: torch.Tensor) -> torch.Tensor:
+    return t if (t.shape[-1] == 1 or t.stride(-1) == 1) else t.contiguous()
+
+
+def _check_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
+    if q.dim() != 3 or k.shape != q.shape or v.shape != q.shape:
+        raise ValueError(f"q, k, v must share one [B, N, d] shape; got "
+                         f"{tuple(q.shape)}, {tuple(k.shape)}, {tuple(v.shape)}")
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise RuntimeError("tarmac_b200 kernels need CUDA tensors (there is no "
+                           "CPU implementation)")
+    if not (q.device == k.device == v.device):
+        raise ValueError("q, k, v must be on one device")
+    if not (q.dtype == k.dtype == v.dtype) or q.dtype not in _DTYPES:
+        raise TypeError(f"q, k, v must all be float32 or bfloat16; got "
+                        f"{q.dtype}, {k.dtype}, {v.dtype}")
+    return _unit_inner(q), _unit_inner(k), _unit_inner(v)
+
+
+def _strides(q, k, v, o) -> ctypes.Array:
+    arr = (ctypes.c_int64 * 8)(q.stride(0), q.stride(1), k.stride(0),
+                               k.stride(1), v.stride(0), v.stride(1),
+                               o.stride(0), o.stride(1))
+    return arr
+
+
+def _scale(d: int, scale: float | None) -> float:
+    return default_scale(d) if scale is None else float(scale)
+
+
+def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                    scale: float | None = None) -> torch.Tensor:
+    """softmax(q k^T * scale, diagonal excluded) v."""
+    q, k, v = _check_qkv(q, k, v)
+    B, N, d = q.shape
+    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    if N < 2:
+        return out.fill_(float("nan"))
+    strides = _strides(q, k, v, out)  # must outlive the call
+    with torch.cuda.device(q.device):
+        _lib.call("tarmac_dense_attention", _ptr(q), _ptr(k), _ptr(v),
+                  _ptr(out), ctypes.addressof(strides), B, N, d,
+                  _DTYPES[q.dtype], _scale(d, scale), _stream(q.device))
+    return out
+
+
+def topk_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                   topk: int, mode: str = "argmax", scale: float | None = None,
+                   return_indices: bool = False):
+    """Fused score-then-select top-k attention.
+
+    ``mode``: ``"argmax"`` (lowest index wins a tie at the k-th score),
+    ``"sort"`` (highest index wins) or ``"threshold"`` (every tied peer kept).
+    ``topk`` must already lie in [1, N-1]. With ``return_indices`` also returns
+    the retained peers, int32 ``[B, N, topk]`` in rank order (k <= 8,
+    argmax/sort only).
+    """
+    q, k, v = _check_qkv(q, k, v)
+    B, N, d = q.shape
+    if mode not in _MODES:
+        raise ValueError(f"unknown selection mode {mode!r}")
+    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    idx = (torch.empty((B, N, topk), device=q.device, dtype=torch.int32)
+           if return_indices else None)
+    strides = _strides(q, k, v, out)
+    with torch.cuda.device(q.device):
+        _lib.call("tarmac_topk_attention", _ptr(q), _ptr(k), _ptr(v),
+                  _ptr(out), ctypes.addressof(strides), B, N, d,
+                  _DTYPES[q.dtype], _scale(d, scale), int(topk), _MODES[mode],
+                  _ptr(idx), _stream(q.device))
+    return (out, idx) if return_indices else out
+
+
+def streaming_topk_attention(q: torch.Tensor, k: torch.Tensor,
+                             v: torch.Tensor, topk: int,
+                             scale: float | None = None,
+                             return_indices: bool = False):
+    """Exact top-k (k <= 8, lowest index wins a tie) with keys streamed
+    through shared memory; no cap on N."""
+    q, k, v = _check_qkv(q, k, v)
+    B, N, d = q.shape
+    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    idx = (torch.empty((B, N, topk), device=q.device, dtype=torch.int32)
+           if return_indices else None)
+    strides = _strides(q, k, v, out)
+    with torch.cuda.device(q.device):
+        _lib.call("tarmac_streaming_topk_attention", _ptr(q), _ptr(k), _ptr(v),
+                  _ptr(out), ctypes.addressof(strides), B, N, d,
+                  _DTYPES[q.dtype], _scale(d, scale), int(topk), _ptr(idx),
+                  _stream(q.device))
+    return (out, idx) if return_indices else out
+
+
+def prescore_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                       idx: torch.Tensor,
+                       scale: float | None = None) -> torch.Tensor:
+    """Attention over the peers named by ``idx`` ([B, N, kk], int64 or int32).
+    Rows naming a peer outside [0, N) come back as NaN."""
+    q, k, v = _check_qkv(q, k, v)
+    B, N, d = q.shape
+    if idx.dim() != 3 or tuple(idx.shape[:2]) != (B, N):
+        raise ValueError(f"idx must be [B, N, kk]; got {tuple(idx.shape)}")
+    if idx.dtype not in (torch.int64, torch.int32):
+        raise TypeError(f"idx must be int64 or int32; got {idx.dtype}")
+    if idx.device != q.device:
+        raise ValueError("idx must be on the device of q")
+    idx = idx.contiguous()
+    kk = idx.shape[-1]
+    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    if kk == 0:
+        return out.fill_(float("nan"))
+    strides = _strides(q, k, v, out)
+    with torch.cuda.device(q.device):
+        _lib.call("tarmac_prescore_attention", _ptr(q), _ptr(k), _ptr(v),
+                  _ptr(out), ctypes.addressof(strides), _ptr(idx),
+                  int(idx.dtype == torch.int64), kk, B, N, d,
+                  _DTYPES[q.dtype], _scale(d, scale), _stream(q.device))
+    return out
+
+
+def _check_pos(pos: torch.Tensor) -> torch.Tensor:
+    if pos.dim() != 3 or pos.shape[-1] != 2:
+        raise ValueError(f"pos must be [B, N, 2]; got {tuple(pos.shape)}")
+    if not pos.is_cuda:
+        raise RuntimeError("tarmac_b200 kernels need CUDA tensors")
+    if pos.dtype != torch.float32:
+        raise TypeError(f"pos must be float32; got {pos.dtype}")
+    return pos.contiguous()
+
+
+def morton_code(pos: torch.Tensor, bits: int = 10) -> torch.Tensor:
+    """Per-episode Morton codes, int64 [B, N]."""
+    pos = _check_pos(pos)
+    B, N, _ = pos.shape
+    out = torch.empty((B, N), device=pos.device, dtype=torch.int64)
+    with torch.cuda.device(pos.device):
+        _lib.call("tarmac_morton_code", _ptr(pos), B, N, int(bits), _ptr(out),
+                  _stream(pos.device))
+    return out
+
+
+def morton_select(pos: torch.Tensor, k: int, bits: int = 10) -> torch.Tensor:
+    """Z-order window peers, int64 [B, N, k] (stable order on equal codes)."""
+    pos = _check_pos(pos)
+    B, N, _ = pos.shape
+    out = torch.empty((B, N, k), device=pos.device, dtype=torch.int64)
+    with torch.cuda.device(pos.device):
+        _lib.call("tarmac_morton_select", _ptr(pos), B, N, int(k), int(bits),
+                  _ptr(out), _stream(pos.device))
+    return out
+
+
+def morton_prescore_attention(q: torch.Tensor, k: torch.Tensor,
+                              v: torch.Tensor, pos: torch.Tensor, topk: int,
+                              bits: int = 10, scale: float | None = None,
+                              return_indices: bool = False):
+    """Fused Z-order selection + attention over the selected peers."""
+    q, k, v = _check_qkv(q, k, v)
+    pos = _check_pos(pos)
+    B, N, d = q.shape
+    if tuple(pos.shape[:2]) != (B, N):
+        raise ValueError("pos must be [B, N, 2] matching q")
+    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    idx = (torch.empty((B, N, topk), device=q.device, dtype=torch.int64)
+           if return_indices else None)
+    strides = _strides(q, k, v, out)
+    with torch.cuda.device(q.device):
+        _lib.call("tarmac_morton_prescore_attention", _ptr(q), _ptr(k),
+                  _ptr(v), _ptr(out), ctypes.addressof(strides), _ptr(pos),
+                  B, N, d, _DTYPES[q.dtype], _scale(d, scale), int(topk),
+                  int(bits), _ptr(idx), _stream(q.device))
+    return (out, idx) if return_indices else out
