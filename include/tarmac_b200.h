@@ -24,7 +24,8 @@
  *   softmax over the retained peers of row i; out[b,i,:] = sum_j w_ij v[b,j,:].
  * Scores and accumulation are fp32 for both dtypes (bf16 inputs are widened).
  *
- * Row-count and width limits: 2 <= N, 1 <= d <= 128.
+ * Row-count and width limits: 2 <= N, 1 <= d <= 128; `scale` must be positive
+ * and finite (TARMAC_ERR_SHAPE otherwise).
  */
 #ifndef TARMAC_B200_H
 #define TARMAC_B200_H

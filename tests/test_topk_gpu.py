@@ -112,6 +112,26 @@ def test_streaming_large_n(ops, N, k):
     check_topk(q, kt, v, k, out, idx=idx)
 
 
+@pytest.mark.parametrize("N,d,k,mode,tie", [
+    (4096, 16, 2, "argmax", "low"), (3000, 16, 5, "argmax", "low"),
+    (512, 128, 2, "argmax", "low"), (700, 100, 3, "sort", "high"),
+    (4096, 16, 1, "sort", "high")])
+def test_keys_beyond_shared_memory_use_streaming_tiles(ops, N, d, k, mode, tie):
+    """Episodes whose keys do not fit the chunked kernel's shared memory run
+    on the tiled streaming kernel; same function."""
+    q, kt, v = qkv(2, N, d, seed=N + d + k)
+    out, idx = ops.topk_attention(q, kt, v, k, mode=mode, return_indices=True)
+    check_topk(q, kt, v, k, out, tie=tie, idx=idx)
+
+
+@pytest.mark.parametrize("k", [1, 2, 3, 4, 5, 6, 7, 8])
+@pytest.mark.parametrize("mode,tie", [("argmax", "low"), ("sort", "high")])
+def test_every_small_k_and_tie_rule(ops, k, mode, tie):
+    q, kt, v = qkv(8, 200, 16, seed=31 * k)
+    out, idx = ops.topk_attention(q, kt, v, k, mode=mode, return_indices=True)
+    check_topk(q, kt, v, k, out, tie=tie, idx=idx)
+
+
 @pytest.mark.parametrize("N,d,k", [(512, 16, 1), (512, 16, 2), (1024, 16, 4),
                                    (128, 32, 2), (512, 64, 1)])
 def test_bf16_inputs(ops, N, d, k):

@@ -6,14 +6,29 @@
 #include <math.h>
 
 #include "common.cuh"
+#include "topk_chunk.cuh"
 
 namespace tarmac {
 cudaError_t launch_topk_stream_f32(const AttnParams& p, bool tie_high,
                                    cudaStream_t s);
 cudaError_t launch_topk_stream_bf16(const AttnParams& p, bool tie_high,
                                     cudaStream_t s);
-static cudaError_t launch_topk_stream(const AttnParams& p, int dtype,
-                                      bool tie_high, cudaStream_t s) {
+cudaError_t launch_topk_chunk_f32_low(const AttnParams& p, cudaStream_t s);
+cudaError_t launch_topk_chunk_f32_high(const AttnParams& p, cudaStream_t s);
+cudaError_t launch_topk_chunk_bf16_low(const AttnParams& p, cudaStream_t s);
+cudaError_t launch_topk_chunk_bf16_high(const AttnParams& p, cudaStream_t s);
+
+// k <= 8 with the lowest- or highest-index tie rule: the chunked kernel when
+// the episode's keys fit its shared memory, else the streaming kernel.
+static cudaError_t launch_topk_small_k(const AttnParams& p, int dtype,
+                                       bool tie_high, cudaStream_t s) {
+  if (chunk_fits(p.N, p.d, p.topk)) {
+    if (dtype == TARMAC_BF16)
+      return tie_high ? launch_topk_chunk_bf16_high(p, s)
+                      : launch_topk_chunk_bf16_low(p, s);
+    return tie_high ? launch_topk_chunk_f32_high(p, s)
+                    : launch_topk_chunk_f32_low(p, s);
+  }
   return dtype == TARMAC_BF16 ? launch_topk_stream_bf16(p, tie_high, s)
                               : launch_topk_stream_f32(p, tie_high, s);
 }
@@ -48,6 +63,7 @@ static int fill_params(AttnParams& p, const void* q, const void* k,
   if (!q || !k || !v || !out) return TARMAC_ERR_NULL;
   if (dtype != TARMAC_F32 && dtype != TARMAC_BF16) return TARMAC_ERR_DTYPE;
   if (B < 0 || N < 2 || d < 1 || d > MAX_D) return TARMAC_ERR_SHAPE;
+  if (!(scale > 0.f) || isinf(scale)) return TARMAC_ERR_SHAPE;
   const int es = elem_size(dtype);
   if (!aligned(q, es) || !aligned(k, es) || !aligned(v, es) || !aligned(out, es))
     return TARMAC_ERR_ALIGN;
@@ -142,7 +158,7 @@ int tarmac_topk_attention(const void* q, const void* k, const void* v,
   cudaStream_t s = (cudaStream_t)stream;
   if (reg)
     return launch_status(
-        launch_topk_stream(p, dtype, mode == TARMAC_SELECT_SORT, s));
+        launch_topk_small_k(p, dtype, mode == TARMAC_SELECT_SORT, s));
   return launch_status(launch_topk_rows(p, dtype, s));
 }
 
@@ -160,7 +176,7 @@ int tarmac_streaming_topk_attention(const void* q, const void* k,
   p.idx_out = idx_out;
   if (B == 0) return TARMAC_OK;
   return launch_status(
-      launch_topk_stream(p, dtype, false, (cudaStream_t)stream));
+      launch_topk_small_k(p, dtype, false, (cudaStream_t)stream));
 }
 
 int tarmac_prescore_attention(const void* q, const void* k, const void* v,

@@ -48,7 +48,9 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
   int qi[QPT];
   float q[QPT][DP];
   float acc[QPT][DP];
-  float m[QPT], l[QPT];
+  float mc2[QPT];  // reference maximum times c2 (exponent units)
+  float mth[QPT];  // raw score above which the reference point moves
+  float l[QPT];
 #pragma unroll
   for (int r = 0; r < QPT; ++r) {
     qi[r] = g * 32 * QPT + r * 32 + lane;
@@ -62,7 +64,8 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
     }
 #pragma unroll
     for (int c = 0; c < DP; ++c) acc[r][c] = 0.f;
-    m[r] = -1e30f;
+    mc2[r] = -1e30f;     // finite, so exp2(fma(-inf, c2, -mc2)) is 0, not NaN
+    mth[r] = -INFINITY;  // the first finite score moves the reference point
     l[r] = 0.f;
   }
 
@@ -95,15 +98,21 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
       float pr[QPT];
 #pragma unroll
       for (int r = 0; r < QPT; ++r) {
-        const float t = (j == qi[r]) ? -INFINITY : s[r] * c2;
-        if (t > m[r] + RESCALE_LOG2) {
-          const float alpha = exp2f(m[r] - t);
+        // m is the reference score (raw units), mc2 = m * c2 rounded once and
+        // shared by the whole row: the exponent fma(s, c2, -mc2) is exact up
+        // to one rounding of a small number, and the rounding of mc2 is a
+        // common factor that the final division cancels.
+        const float sv = (j == qi[r]) ? -INFINITY : s[r];
+        if (sv > mth[r]) {
+          const float mc2n = sv * c2;
+          const float alpha = exp2f(mc2[r] - mc2n);
           l[r] *= alpha;
 #pragma unroll
           for (int c = 0; c < DP; ++c) acc[r][c] *= alpha;
-          m[r] = t;
+          mc2[r] = mc2n;
+          mth[r] = sv + RESCALE_LOG2 / c2;
         }
-        pr[r] = exp2f(t - m[r]);
+        pr[r] = exp2f(fmaf(sv, c2, -mc2[r]));
         l[r] += pr[r];
       }
 #pragma unroll

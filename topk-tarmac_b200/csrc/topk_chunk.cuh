@@ -1,0 +1,400 @@
+// topk_chunk.cuh — resident-key chunked top-k attention (k <= 8) on sm_100a.
+//
+// Same function as the streaming register-buffer kernel (reference:
+// src/kernels/fused_topk_attention.py:211-289, streaming_topk_attention.py:
+// 66-179; lowest or highest index wins a tie at the k-th score), organised so
+// that selection costs about one instruction per score instead of a compare,
+// a branch and a divergent buffer insertion:
+//
+// * The episode's K rows are staged once into shared memory (fp32, rows padded
+//   to DP+4 floats). A block owns 32*QPT queries (QPT per lane, q in
+//   registers as fp32 pairs) and its 4 warps split the keys into contiguous
+//   ranges of 16-key chunks.
+// * Scores use the packed fp32x2 FMA (fma.rn.f32x2): even and odd columns
+//   accumulate in the two halves and are added at the end, so the FMA pipe
+//   does 2 FMAs per issue slot and leaves slots for the selection.
+// * Per query and chunk only the chunk maximum is formed (three-input max),
+//   and a branch-free running buffer keeps the k+1 best chunks (ordered by
+//   (max, chunk index) with the tie rule). The k best scores lie in the k best
+//   chunks: every chunk outside them has k chunk maxima above its own. One
+//   extra chunk covers the diagonal score, which the main loop does not mask
+//   (it can only inflate its own chunk's maximum).
+// * The warps' chunk lists are merged through shared memory; each lane then
+//   recomputes — bit-identically — the scores of its query's k+1 candidate
+//   chunks, drops the diagonal, and keeps the k best by (score, index) with
+//   the tie rule. Only scores >= the (k+1)-th chunk maximum (a lower bound of
+//   the k-th score) reach the exact buffer.
+#pragma once
+
+#include "topk_stream.cuh"
+
+namespace tarmac {
+
+constexpr int CH = 16;       // keys per chunk
+constexpr int CH_WARPS = 4;  // warps per block (they split the keys)
+
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ float hsum2(uint64_t x) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(x));
+  return lo + hi;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// q (as DP/2 column pairs) . one fp32 key row in shared memory (16B aligned).
+// The main loop and the final recompute both call this, so a score is
+// bit-identical wherever it is formed.
+template <int DP>
+__device__ __forceinline__ float dot_pairs(const uint64_t (&qp)[DP / 2],
+                                           const float* kr) {
+  uint64_t acc = 0ull;
+#pragma unroll
+  for (int c = 0; c < DP; c += 4) {
+    const ulonglong2 kv = *reinterpret_cast<const ulonglong2*>(kr + c);
+    acc = ffma2(qp[c / 2], kv.x, acc);
+    acc = ffma2(qp[c / 2 + 1], kv.y, acc);
+  }
+  return hsum2(acc);
+}
+
+// (a, ia) precedes (b, ib) in the retained order: score descending, ties by
+// index ascending (lowest wins) or descending (highest wins); an empty slot
+// (ib < 0) is preceded by everything.
+template <bool TIE_HIGH>
+__device__ __forceinline__ bool better(float a, int ia, float b, int ib) {
+  return ib < 0 || a > b || (a == b && (TIE_HIGH ? ia > ib : ia < ib));
+}
+
+template <int KM, bool TIE_HIGH>
+__device__ __forceinline__ void ins_idx(float (&bs)[KM], int (&bi)[KM],
+                                        float s, int j) {
+#pragma unroll
+  for (int p = KM - 1; p >= 1; --p) {
+    const bool here = better<TIE_HIGH>(s, j, bs[p], bi[p]);
+    const bool above = better<TIE_HIGH>(s, j, bs[p - 1], bi[p - 1]);
+    const float ns = above ? bs[p - 1] : (here ? s : bs[p]);
+    const int ni = above ? bi[p - 1] : (here ? j : bi[p]);
+    bs[p] = ns;
+    bi[p] = ni;
+  }
+  if (better<TIE_HIGH>(s, j, bs[0], bi[0])) {
+    bs[0] = s;
+    bi[0] = j;
+  }
+}
+
+template <int DP>
+__host__ __device__ constexpr int chunk_row_stride() {
+  return DP + 4;  // padding spreads the recompute's row gathers over banks
+}
+
+template <int DP, int QPT, int KC>
+__host__ __device__ constexpr size_t chunk_smem_bytes(int NC) {
+  return (size_t)NC * CH * chunk_row_stride<DP>() * 4 +
+         (size_t)QPT * CH_WARPS * 32 * KC * 8;
+}
+
+template <int DP, int QPT, int KC, bool TIE_HIGH, typename T>
+__global__ void __launch_bounds__(CH_WARPS * 32)
+    topk_chunk_kernel(AttnParams p, int NC) {
+  constexpr int KS = chunk_row_stride<DP>();
+  constexpr int KM = KC - 1;  // exact buffer: the k best scores (k <= KM)
+  extern __shared__ __align__(16) float smem[];
+  float* sK = smem;
+  float* lv = sK + (size_t)NC * CH * KS;          // [QPT][warps][32][KC]
+  int* li = reinterpret_cast<int*>(lv + QPT * CH_WARPS * 32 * KC);
+
+  const int N = p.N, d = p.d;
+  const int gpe = cdiv(N, 32 * QPT);
+  const int b = blockIdx.x / gpe;
+  const int g = blockIdx.x - b * gpe;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const bool vec = p.vec != 0;
+
+  const T* Q = static_cast<const T*>(p.q) + (int64_t)b * p.st.qb;
+  const T* K = static_cast<const T*>(p.k) + (int64_t)b * p.st.kb;
+  const T* V = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
+  T* O = static_cast<T*>(p.o) + (int64_t)b * p.st.ob;
+
+  // ---- stage the episode's keys: rows [0, NC*CH), zero beyond N and d ----
+  {
+    constexpr int C4 = DP / 4;
+    const int total = NC * CH * C4;
+    for (int e = threadIdx.x; e < total; e += blockDim.x) {
+      const int row = e / C4;
+      const int c = (e - row * C4) * 4;
+      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (row < N && c < d) {
+        const T* src = K + (int64_t)row * p.st.kn + c;
+        if (vec) {
+          f = load4(src);
+        } else {
+          f.x = to_f32<T>(src[0]);
+          f.y = (c + 1 < d) ? to_f32<T>(src[1]) : 0.f;
+          f.z = (c + 2 < d) ? to_f32<T>(src[2]) : 0.f;
+          f.w = (c + 3 < d) ? to_f32<T>(src[3]) : 0.f;
+        }
+      }
+      *reinterpret_cast<float4*>(sK + (size_t)row * KS + c) = f;
+    }
+  }
+
+  // ---- queries as column pairs -------------------------------------------
+  uint64_t qp[QPT][DP / 2];
+  int qi[QPT];
+#pragma unroll
+  for (int r = 0; r < QPT; ++r) {
+    qi[r] = g * 32 * QPT + r * 32 + lane;
+    float qr[DP];
+    if (qi[r] < N) {
+      load_row<DP, T>(qr, Q + (int64_t)qi[r] * p.st.qn, d, vec);
+    } else {
+#pragma unroll
+      for (int c = 0; c < DP; ++c) qr[c] = 0.f;
+    }
+#pragma unroll
+    for (int c = 0; c < DP; c += 2)
+      qp[r][c / 2] = pack2(qr[c] * p.qscale, qr[c + 1] * p.qscale);
+  }
+  __syncthreads();
+
+  // ---- main loop: chunk maxima, running k+1 best chunks -------------------
+  float cbv[QPT][KC];
+  int cbi[QPT][KC];
+#pragma unroll
+  for (int r = 0; r < QPT; ++r)
+#pragma unroll
+    for (int m = 0; m < KC; ++m) {
+      cbv[r][m] = -INFINITY;
+      cbi[r][m] = -1;
+    }
+  const int c0 = (warp * NC) / CH_WARPS;
+  const int c1 = ((warp + 1) * NC) / CH_WARPS;
+  for (int c = c0; c < c1; ++c) {
+    const float* kb = sK + (size_t)c * CH * KS;
+    float cm[QPT];
+#pragma unroll
+    for (int r = 0; r < QPT; ++r) cm[r] = -INFINITY;
+    if ((c + 1) * CH <= N) {
+#pragma unroll 4
+      for (int jj = 0; jj < CH; jj += 2) {
+#pragma unroll
+        for (int r = 0; r < QPT; ++r) {
+          const float s0 = dot_pairs<DP>(qp[r], kb + jj * KS);
+          const float s1 = dot_pairs<DP>(qp[r], kb + (jj + 1) * KS);
+          cm[r] = max3f(cm[r], s0, s1);
+        }
+      }
+    } else {
+      const int nk = N - c * CH;  // partial last chunk
+      for (int jj = 0; jj < nk; ++jj) {
+#pragma unroll
+        for (int r = 0; r < QPT; ++r)
+          cm[r] = fmaxf(cm[r], dot_pairs<DP>(qp[r], kb + jj * KS));
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < QPT; ++r) buf_insert<KC, TIE_HIGH>(cbv[r], cbi[r], cm[r], c);
+  }
+
+  // ---- publish each warp's chunk lists ------------------------------------
+#pragma unroll
+  for (int r = 0; r < QPT; ++r)
+#pragma unroll
+    for (int m = 0; m < KC; ++m) {
+      const int o = ((r * CH_WARPS + warp) * 32 + lane) * KC + m;
+      lv[o] = cbv[r][m];
+      li[o] = cbi[r][m];
+    }
+  __syncthreads();
+  if (warp >= QPT) return;
+
+  // ---- finalize: warp w owns query row r = w of this lane -----------------
+  const int r = warp;
+  const int i = g * 32 * QPT + r * 32 + lane;
+  if (i >= N) return;
+  uint64_t qf[DP / 2];
+  {
+    float qr[DP];
+    load_row<DP, T>(qr, Q + (int64_t)i * p.st.qn, d, vec);
+#pragma unroll
+    for (int c = 0; c < DP; c += 2)
+      qf[c / 2] = pack2(qr[c] * p.qscale, qr[c + 1] * p.qscale);
+  }
+  float mv[KC];
+  int mi[KC];
+#pragma unroll
+  for (int m = 0; m < KC; ++m) {
+    mv[m] = -INFINITY;
+    mi[m] = -1;
+  }
+  for (int w2 = 0; w2 < CH_WARPS; ++w2) {
+#pragma unroll
+    for (int m = 0; m < KC; ++m) {
+      const int o = ((r * CH_WARPS + w2) * 32 + lane) * KC + m;
+      const int id = li[o];
+      if (id >= 0) ins_idx<KC, TIE_HIGH>(mv, mi, lv[o], id);
+    }
+  }
+  const float thr = mv[KC - 1];  // <= the k-th best score of the row
+  float bs[KM];
+  int bi[KM];
+#pragma unroll
+  for (int m = 0; m < KM; ++m) {
+    bs[m] = -INFINITY;
+    bi[m] = -1;
+  }
+#pragma unroll
+  for (int m = 0; m < KC; ++m) {
+    const int cid = mi[m];
+    if (cid < 0) continue;
+    const int jend = min(CH, N - cid * CH);
+    for (int jj = 0; jj < jend; ++jj) {
+      const int j = cid * CH + jj;
+      if (j == i) continue;
+      const float s = dot_pairs<DP>(qf, sK + (size_t)j * KS);
+      if (s >= thr) ins_idx<KM, TIE_HIGH>(bs, bi, s, j);
+    }
+  }
+
+  // ---- softmax over the k retained scores, V gather-aggregate -------------
+  const int kk = p.topk;
+  const float mx = bs[0] * p.post_scale;
+  float den = 0.f;
+  float e[KM];
+  bool empty = false;
+#pragma unroll
+  for (int m = 0; m < KM; ++m) {
+    e[m] = (m < kk) ? expf(bs[m] * p.post_scale - mx) : 0.f;
+    den += e[m];
+    empty |= (m < kk) && (bi[m] < 0);
+  }
+  float acc[DP];
+#pragma unroll
+  for (int c = 0; c < DP; ++c) acc[c] = 0.f;
+#pragma unroll
+  for (int m = 0; m < KM; ++m) {
+    if (m < kk && !empty) {
+      const float w = e[m] / den;
+      const T* vr = V + (int64_t)bi[m] * p.st.vn;
+#pragma unroll
+      for (int c = 0; c < DP; c += 4) {
+        if (c < d) {
+          float4 f;
+          if (vec) {
+            f = load4(vr + c);
+          } else {
+            f.x = to_f32<T>(vr[c]);
+            f.y = (c + 1 < d) ? to_f32<T>(vr[c + 1]) : 0.f;
+            f.z = (c + 2 < d) ? to_f32<T>(vr[c + 2]) : 0.f;
+            f.w = (c + 3 < d) ? to_f32<T>(vr[c + 3]) : 0.f;
+          }
+          acc[c] = fmaf(w, f.x, acc[c]);
+          acc[c + 1] = fmaf(w, f.y, acc[c + 1]);
+          acc[c + 2] = fmaf(w, f.z, acc[c + 2]);
+          acc[c + 3] = fmaf(w, f.w, acc[c + 3]);
+        }
+      }
+    }
+  }
+  if (empty) {
+#pragma unroll
+    for (int c = 0; c < DP; ++c) acc[c] = __int_as_float(0x7fc00000);
+  }
+  store_row<DP, T>(O + (int64_t)i * p.st.on, acc, d, vec);
+  if (p.idx_out != nullptr) {
+    int32_t* io = p.idx_out + ((int64_t)b * N + i) * kk;
+#pragma unroll
+    for (int m = 0; m < KM; ++m)
+      if (m < kk) io[m] = bi[m];
+  }
+}
+
+// QPT query rows per lane: q pairs (QPT * DP regs) plus 2 * QPT * KC chunk
+// slots must stay within the register budget.
+template <int DP, int KC>
+constexpr int chunk_qpt() {
+  return DP >= 64 ? 1 : (DP >= 32 ? (KC >= 9 ? 1 : 2) : (KC >= 9 ? 2 : 4));
+}
+
+// Largest dynamic shared memory the chunked kernel may take per block.
+constexpr size_t CHUNK_SMEM_MAX = 200 * 1024;
+
+constexpr int chunk_slots(int topk) {
+  return topk <= 1 ? 2 : (topk <= 2 ? 3 : (topk <= 4 ? 5 : 9));
+}
+
+template <int DP, int KC>
+size_t chunk_smem_for(int N) {
+  return chunk_smem_bytes<DP, chunk_qpt<DP, KC>(), KC>(cdiv(N, CH));
+}
+
+template <int DP>
+size_t chunk_smem_dp(int N, int topk) {
+  switch (chunk_slots(topk)) {
+    case 2: return chunk_smem_for<DP, 2>(N);
+    case 3: return chunk_smem_for<DP, 3>(N);
+    case 5: return chunk_smem_for<DP, 5>(N);
+    default: return chunk_smem_for<DP, 9>(N);
+  }
+}
+
+// true when the episode's keys fit the chunked kernel's shared memory
+inline bool chunk_fits(int N, int d, int topk) {
+  size_t sm;
+  if (d <= 16) sm = chunk_smem_dp<16>(N, topk);
+  else if (d <= 32) sm = chunk_smem_dp<32>(N, topk);
+  else if (d <= 64) sm = chunk_smem_dp<64>(N, topk);
+  else sm = chunk_smem_dp<128>(N, topk);
+  return sm <= CHUNK_SMEM_MAX;
+}
+
+template <int DP, int KC, bool TIE_HIGH, typename T>
+cudaError_t launch_chunk_t(const AttnParams& p, cudaStream_t s) {
+  constexpr int QPT = chunk_qpt<DP, KC>();
+  const int NC = cdiv(p.N, CH);
+  const size_t sm = chunk_smem_bytes<DP, QPT, KC>(NC);
+  cudaError_t e = cudaFuncSetAttribute(
+      topk_chunk_kernel<DP, QPT, KC, TIE_HIGH, T>,
+      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = (int64_t)p.B * cdiv(p.N, 32 * QPT);
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  topk_chunk_kernel<DP, QPT, KC, TIE_HIGH, T>
+      <<<(unsigned)blocks, CH_WARPS * 32, sm, s>>>(p, NC);
+  return cudaGetLastError();
+}
+
+template <int DP, bool TIE_HIGH, typename T>
+cudaError_t launch_chunk_kc(const AttnParams& p, cudaStream_t s) {
+  switch (chunk_slots(p.topk)) {
+    case 2: return launch_chunk_t<DP, 2, TIE_HIGH, T>(p, s);
+    case 3: return launch_chunk_t<DP, 3, TIE_HIGH, T>(p, s);
+    case 5: return launch_chunk_t<DP, 5, TIE_HIGH, T>(p, s);
+    default: return launch_chunk_t<DP, 9, TIE_HIGH, T>(p, s);
+  }
+}
+
+// One element type and tie rule per translation unit (compile in parallel).
+template <bool TIE_HIGH, typename T>
+cudaError_t launch_chunk_dt(const AttnParams& p, cudaStream_t s) {
+  if (p.d <= 16) return launch_chunk_kc<16, TIE_HIGH, T>(p, s);
+  if (p.d <= 32) return launch_chunk_kc<32, TIE_HIGH, T>(p, s);
+  if (p.d <= 64) return launch_chunk_kc<64, TIE_HIGH, T>(p, s);
+  return launch_chunk_kc<128, TIE_HIGH, T>(p, s);
+}
+
+}  // namespace tarmac
