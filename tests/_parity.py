@@ -33,9 +33,13 @@ def tol_for(dtype) -> dict:
     return BF16_TOL if dtype == torch.bfloat16 else FP32_TOL
 
 
-def check_topk(q, k, v, topk, out, tie="low", idx=None, max_amb_frac=1e-3):
+def check_topk(q, k, v, topk, out, tie="low", idx=None, max_amb_frac=1e-2):
     """Compare a top-k attention output (and optional rank-ordered indices)
     with the oracle on every unambiguous row; returns the ambiguous-row count.
+
+    Ambiguous rows (k-th and (k+1)-th exact scores closer than fp32 rounding
+    of a length-d dot product) are expected at about 0.1 % of rows when k
+    sits in the dense middle of a score row; more than 1 % fails the test.
     """
     qn, kn, vn = host(q), host(k), host(v)
     ref, mask = oracle.topk_attention(qn, kn, vn, topk, tie=tie)

@@ -126,6 +126,52 @@ __device__ __forceinline__ void store_row(T* p, const float (&x)[DP], int d,
     if (c < d) p[c] = from_f32<T>(x[c]);
 }
 
+// ---------------------------------------------------------------------------
+// packed fp32x2 arithmetic (sm_100): one instruction performs two IEEE fp32
+// FMAs, which halves the issue slots the FMA-bound loops spend on arithmetic
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ float2 unpack2(uint64_t x) {
+  float lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(x));
+  return make_float2(lo, hi);
+}
+__device__ __forceinline__ float hsum2(uint64_t x) {
+  const float2 f = unpack2(x);
+  return f.x + f.y;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// q (as DP/2 column pairs) . one fp32 row in shared memory (16-byte aligned):
+// even and odd columns accumulate in the two halves, added at the end. Every
+// caller forms a given score through this one function, so a score is
+// bit-identical wherever it is recomputed.
+template <int DP>
+__device__ __forceinline__ float dot_pairs(const uint64_t (&qp)[DP / 2],
+                                           const float* kr) {
+  uint64_t acc = 0ull;
+#pragma unroll
+  for (int c = 0; c < DP; c += 4) {
+    const ulonglong2 kv = *reinterpret_cast<const ulonglong2*>(kr + c);
+    acc = ffma2(qp[c / 2], kv.x, acc);
+    acc = ffma2(qp[c / 2 + 1], kv.y, acc);
+  }
+  return hsum2(acc);
+}
+
 // Monotone map fp32 -> uint32: a < b (as non-NaN floats) iff key(a) < key(b).
 // Restates _float_to_ordered_int (fused_topk_attention.py:113-124) in unsigned
 // form (offset by 2^31, so the order is the same).

@@ -4,11 +4,13 @@
 // (src/kernels/fused_dense_attention.py:38-99): softmax(q k^T * scale) v with
 // the diagonal excluded and no score matrix written. The design differs:
 // one thread owns QPT query rows; K and V tiles are staged through shared
-// memory and read with broadcast loads; the online softmax works in base 2
-// and only moves its reference maximum when a score exceeds it by more than
-// 2^RESCALE_LOG2 (a stale maximum leaves every weight bounded by 2^8, so the
-// normaliser cannot overflow, and the final division makes the result
-// independent of the reference point).
+// memory and read with broadcast loads; both products run on the packed
+// fp32x2 FMA (q.k with even/odd column halves, p*v with the weight duplicated
+// into both halves); the online softmax works in base 2 and only moves its
+// reference maximum when a score exceeds it by more than 2^RESCALE_LOG2 (a
+// stale maximum leaves every weight bounded by 2^8, so the normaliser cannot
+// overflow, and the final division makes the result independent of the
+// reference point).
 #include "common.cuh"
 
 namespace tarmac {
@@ -24,6 +26,7 @@ __host__ __device__ constexpr int dense_tile_keys() {
 template <int DP, int QPT, typename T>
 __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
   constexpr int TK = dense_tile_keys<DP>();
+  constexpr int H = DP / 2;  // column pairs
   __shared__ __align__(16) float sk[TK * DP];
   __shared__ __align__(16) float sv[TK * DP];
 
@@ -46,24 +49,26 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
   // scores enter the exponent as s * scale * log2(e)
   const float c2 = p.post_scale * LOG2E;
   int qi[QPT];
-  float q[QPT][DP];
-  float acc[QPT][DP];
+  uint64_t qp[QPT][H];
+  uint64_t acc[QPT][H];
   float mc2[QPT];  // reference maximum times c2 (exponent units)
   float mth[QPT];  // raw score above which the reference point moves
   float l[QPT];
 #pragma unroll
   for (int r = 0; r < QPT; ++r) {
     qi[r] = g * 32 * QPT + r * 32 + lane;
+    float qr[DP];
     if (active && qi[r] < N) {
-      load_row<DP, T>(q[r], Q + (int64_t)qi[r] * p.st.qn, d, vec);
-#pragma unroll
-      for (int c = 0; c < DP; ++c) q[r][c] *= p.qscale;
+      load_row<DP, T>(qr, Q + (int64_t)qi[r] * p.st.qn, d, vec);
     } else {
 #pragma unroll
-      for (int c = 0; c < DP; ++c) q[r][c] = 0.f;
+      for (int c = 0; c < DP; ++c) qr[c] = 0.f;
     }
 #pragma unroll
-    for (int c = 0; c < DP; ++c) acc[r][c] = 0.f;
+    for (int c = 0; c < DP; c += 2) {
+      qp[r][c / 2] = pack2(qr[c] * p.qscale, qr[c + 1] * p.qscale);
+      acc[r][c / 2] = 0ull;
+    }
     mc2[r] = -1e30f;     // finite, so exp2(fma(-inf, c2, -mc2)) is 0, not NaN
     mth[r] = -INFINITY;  // the first finite score moves the reference point
     l[r] = 0.f;
@@ -80,50 +85,37 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
     for (int jj = 0; jj < nk; ++jj) {
       const float* kr = sk + jj * DP;
       const float* vr = sv + jj * DP;
-      float s[QPT];
-#pragma unroll
-      for (int r = 0; r < QPT; ++r) s[r] = 0.f;
-#pragma unroll
-      for (int c = 0; c < DP; c += 4) {
-        const float4 kv = *reinterpret_cast<const float4*>(kr + c);
-#pragma unroll
-        for (int r = 0; r < QPT; ++r) {
-          s[r] = fmaf(q[r][c], kv.x, s[r]);
-          s[r] = fmaf(q[r][c + 1], kv.y, s[r]);
-          s[r] = fmaf(q[r][c + 2], kv.z, s[r]);
-          s[r] = fmaf(q[r][c + 3], kv.w, s[r]);
-        }
-      }
       const int j = t0 + jj;
-      float pr[QPT];
+      uint64_t pp[QPT];
 #pragma unroll
       for (int r = 0; r < QPT; ++r) {
-        // m is the reference score (raw units), mc2 = m * c2 rounded once and
-        // shared by the whole row: the exponent fma(s, c2, -mc2) is exact up
-        // to one rounding of a small number, and the rounding of mc2 is a
-        // common factor that the final division cancels.
-        const float sv = (j == qi[r]) ? -INFINITY : s[r];
-        if (sv > mth[r]) {
-          const float mc2n = sv * c2;
+        // m is kept as mc2 = m * c2, rounded once and shared by the whole row:
+        // the exponent fma(s, c2, -mc2) then carries one rounding of a small
+        // number, and the rounding of mc2 is a common factor the final
+        // division cancels.
+        const float s = dot_pairs<DP>(qp[r], kr);
+        const float sv_ = (j == qi[r]) ? -INFINITY : s;
+        if (sv_ > mth[r]) {
+          const float mc2n = sv_ * c2;
           const float alpha = exp2f(mc2[r] - mc2n);
           l[r] *= alpha;
+          const uint64_t aa = pack2(alpha, alpha);
 #pragma unroll
-          for (int c = 0; c < DP; ++c) acc[r][c] *= alpha;
+          for (int h = 0; h < H; ++h) acc[r][h] = ffma2(acc[r][h], aa, 0ull);
           mc2[r] = mc2n;
-          mth[r] = sv + RESCALE_LOG2 / c2;
+          mth[r] = sv_ + RESCALE_LOG2 / c2;
         }
-        pr[r] = exp2f(fmaf(sv, c2, -mc2[r]));
-        l[r] += pr[r];
+        const float pe = exp2f(fmaf(sv_, c2, -mc2[r]));
+        l[r] += pe;
+        pp[r] = pack2(pe, pe);
       }
 #pragma unroll
       for (int c = 0; c < DP; c += 4) {
-        const float4 vv = *reinterpret_cast<const float4*>(vr + c);
+        const ulonglong2 vv = *reinterpret_cast<const ulonglong2*>(vr + c);
 #pragma unroll
         for (int r = 0; r < QPT; ++r) {
-          acc[r][c] = fmaf(pr[r], vv.x, acc[r][c]);
-          acc[r][c + 1] = fmaf(pr[r], vv.y, acc[r][c + 1]);
-          acc[r][c + 2] = fmaf(pr[r], vv.z, acc[r][c + 2]);
-          acc[r][c + 3] = fmaf(pr[r], vv.w, acc[r][c + 3]);
+          acc[r][c / 2] = ffma2(pp[r], vv.x, acc[r][c / 2]);
+          acc[r][c / 2 + 1] = ffma2(pp[r], vv.y, acc[r][c / 2 + 1]);
         }
       }
     }
@@ -135,7 +127,11 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
     const float inv = 1.0f / l[r];
     float o[DP];
 #pragma unroll
-    for (int c = 0; c < DP; ++c) o[c] = acc[r][c] * inv;
+    for (int h = 0; h < H; ++h) {
+      const float2 f = unpack2(acc[r][h]);
+      o[2 * h] = f.x * inv;
+      o[2 * h + 1] = f.y * inv;
+    }
     store_row<DP, T>(O + (int64_t)qi[r] * p.st.on, o, d, vec);
   }
 }

@@ -33,43 +33,6 @@ namespace tarmac {
 constexpr int CH = 16;       // keys per chunk
 constexpr int CH_WARPS = 4;  // warps per block (they split the keys)
 
-__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
-  return r;
-}
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ float hsum2(uint64_t x) {
-  float lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(x));
-  return lo + hi;
-}
-__device__ __forceinline__ float max3f(float a, float b, float c) {
-  float d;
-  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
-  return d;
-}
-
-// q (as DP/2 column pairs) . one fp32 key row in shared memory (16B aligned).
-// The main loop and the final recompute both call this, so a score is
-// bit-identical wherever it is formed.
-template <int DP>
-__device__ __forceinline__ float dot_pairs(const uint64_t (&qp)[DP / 2],
-                                           const float* kr) {
-  uint64_t acc = 0ull;
-#pragma unroll
-  for (int c = 0; c < DP; c += 4) {
-    const ulonglong2 kv = *reinterpret_cast<const ulonglong2*>(kr + c);
-    acc = ffma2(qp[c / 2], kv.x, acc);
-    acc = ffma2(qp[c / 2 + 1], kv.y, acc);
-  }
-  return hsum2(acc);
-}
-
 // (a, ia) precedes (b, ib) in the retained order: score descending, ties by
 // index ascending (lowest wins) or descending (highest wins); an empty slot
 // (ib < 0) is preceded by everything.
@@ -257,16 +220,22 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
     bs[m] = -INFINITY;
     bi[m] = -1;
   }
+  // Each lane walks its own candidate chunks. Chunk bases are bank-aligned,
+  // so every lane starts at a different row of its chunk ((jj + lane) mod CH):
+  // rows r and r+1 sit DP+4 floats apart, which puts 8 consecutive lanes on 8
+  // distinct 4-bank groups. ins_idx orders by (score, index) explicitly, so
+  // the visiting order does not matter.
 #pragma unroll
   for (int m = 0; m < KC; ++m) {
     const int cid = mi[m];
     if (cid < 0) continue;
-    const int jend = min(CH, N - cid * CH);
-    for (int jj = 0; jj < jend; ++jj) {
-      const int j = cid * CH + jj;
-      if (j == i) continue;
+    const int nk = min(CH, N - cid * CH);
+#pragma unroll 4
+    for (int jj = 0; jj < CH; ++jj) {
+      const int jr = (jj + lane) & (CH - 1);
+      const int j = cid * CH + jr;
       const float s = dot_pairs<DP>(qf, sK + (size_t)j * KS);
-      if (s >= thr) ins_idx<KM, TIE_HIGH>(bs, bi, s, j);
+      if (jr < nk && j != i && s >= thr) ins_idx<KM, TIE_HIGH>(bs, bi, s, j);
     }
   }
 
