@@ -184,32 +184,83 @@ __device__ __forceinline__ float key_to_float(uint32_t k) {
   return __uint_as_float(u);
 }
 
-// Stage rows [r0, r0 + nrows) of a [N, d] episode (row stride `rs`) into a
-// shared fp32 tile [TK][DP], zero-padding rows >= N and columns >= d.
+// 16-byte global -> shared copy that does not pass through registers
+// (cp.async, L2 only); completes at cp_async_wait_all().
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int PENDING>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(PENDING) : "memory");
+}
+
+// Stage rows [0, nrows) of a [N, d] episode slice (first row `r0`, row
+// stride `rs`) into shared fp32 rows of `sstride` floats, zero-padding rows
+// >= N and columns >= d. fp32 rows on the vector path move with cp.async
+// (the caller waits with cp_async_wait_all / cp_async_wait<n>); other rows
+// are converted through registers, four 16-byte loads in flight per thread.
 // All threads of the block participate.
-template <int DP, int TK, typename T>
-__device__ __forceinline__ void stage_tile(float* __restrict__ tile,
+template <int DP, typename T>
+__device__ __forceinline__ void stage_rows(float* __restrict__ dst, int sstride,
                                            const T* __restrict__ base,
-                                           int64_t rs, int r0, int N, int d,
-                                           bool vec) {
+                                           int64_t rs, int r0, int nrows, int N,
+                                           int d, bool vec) {
   constexpr int C4 = DP / 4;
-  for (int e = threadIdx.x; e < TK * C4; e += blockDim.x) {
-    int row = e / C4;
-    int c = (e - row * C4) * 4;
-    int r = r0 + row;
-    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (r < N && c < d) {
-      const T* p = base + (int64_t)r * rs + c;
-      if (vec) {
-        f = load4(p);
-      } else {
-        f.x = to_f32<T>(p[0]);
-        f.y = (c + 1 < d) ? to_f32<T>(p[1]) : 0.f;
-        f.z = (c + 2 < d) ? to_f32<T>(p[2]) : 0.f;
-        f.w = (c + 3 < d) ? to_f32<T>(p[3]) : 0.f;
+  const int total = nrows * C4;
+  if constexpr (sizeof(T) == 4) {
+    if (vec) {
+      for (int e = threadIdx.x; e < total; e += blockDim.x) {
+        const int row = e / C4;
+        const int c = (e - row * C4) * 4;
+        float* sp = dst + (size_t)row * sstride + c;
+        const int r = r0 + row;
+        if (r < N && c < d)
+          cp_async16(sp, base + (int64_t)r * rs + c);
+        else
+          *reinterpret_cast<float4*>(sp) = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      return;
+    }
+  }
+  constexpr int U = 4;
+  for (int e0 = threadIdx.x; e0 < total; e0 += U * blockDim.x) {
+    float4 f[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = e0 + u * blockDim.x;
+      const int row = e / C4;
+      const int c = (e - row * C4) * 4;
+      const int r = r0 + row;
+      f[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (e < total && r < N && c < d) {
+        const T* src = base + (int64_t)r * rs + c;
+        if (vec) {
+          f[u] = load4(src);
+        } else {
+          f[u].x = to_f32<T>(src[0]);
+          f[u].y = (c + 1 < d) ? to_f32<T>(src[1]) : 0.f;
+          f[u].z = (c + 2 < d) ? to_f32<T>(src[2]) : 0.f;
+          f[u].w = (c + 3 < d) ? to_f32<T>(src[3]) : 0.f;
+        }
       }
     }
-    *reinterpret_cast<float4*>(tile + row * DP + c) = f;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = e0 + u * blockDim.x;
+      if (e < total) {
+        const int row = e / C4;
+        const int c = (e - row * C4) * 4;
+        *reinterpret_cast<float4*>(dst + (size_t)row * sstride + c) = f[u];
+      }
+    }
   }
 }
 

@@ -23,12 +23,61 @@ __host__ __device__ constexpr int dense_tile_keys() {
   return 8192 / (DP * 4);  // 8 KB of K plus 8 KB of V per tile
 }
 
+// One staged tile of nk keys (rows of DP floats) against QPT query rows.
+template <int DP, int QPT>
+__device__ __forceinline__ void dense_tile(
+    const float* __restrict__ sk, const float* __restrict__ sv, int nk, int t0,
+    const int (&qi)[QPT], const uint64_t (&qp)[QPT][DP / 2],
+    uint64_t (&acc)[QPT][DP / 2], float (&mc2)[QPT], float (&mth)[QPT],
+    float (&l)[QPT], float c2) {
+  constexpr int H = DP / 2;
+#pragma unroll 2
+  for (int jj = 0; jj < nk; ++jj) {
+    const float* kr = sk + jj * DP;
+    const float* vr = sv + jj * DP;
+    const int j = t0 + jj;
+    uint64_t pp[QPT];
+#pragma unroll
+    for (int r = 0; r < QPT; ++r) {
+      // m is kept as mc2 = m * c2, rounded once and shared by the whole row:
+      // the exponent fma(s, c2, -mc2) then carries one rounding of a small
+      // number, and the rounding of mc2 is a common factor the final
+      // division cancels.
+      const float s = dot_pairs<DP>(qp[r], kr);
+      const float sd = (j == qi[r]) ? -INFINITY : s;
+      if (sd > mth[r]) {
+        const float mc2n = sd * c2;
+        const float alpha = exp2f(mc2[r] - mc2n);
+        l[r] *= alpha;
+        const uint64_t aa = pack2(alpha, alpha);
+#pragma unroll
+        for (int h = 0; h < H; ++h) acc[r][h] = ffma2(acc[r][h], aa, 0ull);
+        mc2[r] = mc2n;
+        mth[r] = sd + RESCALE_LOG2 / c2;
+      }
+      const float pe = exp2f(fmaf(sd, c2, -mc2[r]));
+      l[r] += pe;
+      pp[r] = pack2(pe, pe);
+    }
+#pragma unroll
+    for (int c = 0; c < DP; c += 4) {
+      const ulonglong2 vv = *reinterpret_cast<const ulonglong2*>(vr + c);
+#pragma unroll
+      for (int r = 0; r < QPT; ++r) {
+        acc[r][c / 2] = ffma2(pp[r], vv.x, acc[r][c / 2]);
+        acc[r][c / 2 + 1] = ffma2(pp[r], vv.y, acc[r][c / 2 + 1]);
+      }
+    }
+  }
+}
+
 template <int DP, int QPT, typename T>
 __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
   constexpr int TK = dense_tile_keys<DP>();
   constexpr int H = DP / 2;  // column pairs
-  __shared__ __align__(16) float sk[TK * DP];
-  __shared__ __align__(16) float sv[TK * DP];
+  // double-buffered K and V tiles: tile t+1 is in flight while t is used
+  __shared__ __align__(16) float sk[2][TK * DP];
+  __shared__ __align__(16) float sv[2][TK * DP];
 
   const int N = p.N, d = p.d;
   const int groups = cdiv(N, 32 * QPT);
@@ -74,51 +123,26 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
     l[r] = 0.f;
   }
 
-  for (int t0 = 0; t0 < N; t0 += TK) {
-    __syncthreads();
-    stage_tile<DP, TK, T>(sk, K, p.st.kn, t0, N, d, vec);
-    stage_tile<DP, TK, T>(sv, V, p.st.vn, t0, N, d, vec);
-    __syncthreads();
-    if (!active) continue;
-    const int nk = min(TK, N - t0);
-#pragma unroll 2
-    for (int jj = 0; jj < nk; ++jj) {
-      const float* kr = sk + jj * DP;
-      const float* vr = sv + jj * DP;
-      const int j = t0 + jj;
-      uint64_t pp[QPT];
-#pragma unroll
-      for (int r = 0; r < QPT; ++r) {
-        // m is kept as mc2 = m * c2, rounded once and shared by the whole row:
-        // the exponent fma(s, c2, -mc2) then carries one rounding of a small
-        // number, and the rounding of mc2 is a common factor the final
-        // division cancels.
-        const float s = dot_pairs<DP>(qp[r], kr);
-        const float sv_ = (j == qi[r]) ? -INFINITY : s;
-        if (sv_ > mth[r]) {
-          const float mc2n = sv_ * c2;
-          const float alpha = exp2f(mc2[r] - mc2n);
-          l[r] *= alpha;
-          const uint64_t aa = pack2(alpha, alpha);
-#pragma unroll
-          for (int h = 0; h < H; ++h) acc[r][h] = ffma2(acc[r][h], aa, 0ull);
-          mc2[r] = mc2n;
-          mth[r] = sv_ + RESCALE_LOG2 / c2;
-        }
-        const float pe = exp2f(fmaf(sv_, c2, -mc2[r]));
-        l[r] += pe;
-        pp[r] = pack2(pe, pe);
-      }
-#pragma unroll
-      for (int c = 0; c < DP; c += 4) {
-        const ulonglong2 vv = *reinterpret_cast<const ulonglong2*>(vr + c);
-#pragma unroll
-        for (int r = 0; r < QPT; ++r) {
-          acc[r][c / 2] = ffma2(pp[r], vv.x, acc[r][c / 2]);
-          acc[r][c / 2 + 1] = ffma2(pp[r], vv.y, acc[r][c / 2 + 1]);
-        }
-      }
+  const int ntiles = cdiv(N, TK);
+  stage_rows<DP, T>(sk[0], DP, K, p.st.kn, 0, TK, N, d, vec);
+  stage_rows<DP, T>(sv[0], DP, V, p.st.vn, 0, TK, N, d, vec);
+  cp_async_commit();
+  for (int t = 0; t < ntiles; ++t) {
+    const int t0 = t * TK;
+    const int buf = t & 1;
+    if (t + 1 < ntiles) {
+      stage_rows<DP, T>(sk[buf ^ 1], DP, K, p.st.kn, t0 + TK, TK, N, d, vec);
+      stage_rows<DP, T>(sv[buf ^ 1], DP, V, p.st.vn, t0 + TK, TK, N, d, vec);
+      cp_async_commit();
+      cp_async_wait<1>();  // tile t has landed; t+1 may still be in flight
+    } else {
+      cp_async_wait<0>();
     }
+    __syncthreads();
+    if (active)
+      dense_tile<DP, QPT>(sk[buf], sv[buf], min(TK, N - t0), t0, qi, qp, acc,
+                          mc2, mth, l, c2);
+    __syncthreads();  // everyone is done with `buf` before it is refilled
   }
   if (!active) return;
 #pragma unroll

@@ -93,27 +93,7 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
   T* O = static_cast<T*>(p.o) + (int64_t)b * p.st.ob;
 
   // ---- stage the episode's keys: rows [0, NC*CH), zero beyond N and d ----
-  {
-    constexpr int C4 = DP / 4;
-    const int total = NC * CH * C4;
-    for (int e = threadIdx.x; e < total; e += blockDim.x) {
-      const int row = e / C4;
-      const int c = (e - row * C4) * 4;
-      float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (row < N && c < d) {
-        const T* src = K + (int64_t)row * p.st.kn + c;
-        if (vec) {
-          f = load4(src);
-        } else {
-          f.x = to_f32<T>(src[0]);
-          f.y = (c + 1 < d) ? to_f32<T>(src[1]) : 0.f;
-          f.z = (c + 2 < d) ? to_f32<T>(src[2]) : 0.f;
-          f.w = (c + 3 < d) ? to_f32<T>(src[3]) : 0.f;
-        }
-      }
-      *reinterpret_cast<float4*>(sK + (size_t)row * KS + c) = f;
-    }
-  }
+  stage_rows<DP, T>(sK, KS, K, p.st.kn, 0, NC * CH, N, d, vec);
 
   // ---- queries as column pairs -------------------------------------------
   uint64_t qp[QPT][DP / 2];
@@ -132,6 +112,7 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
     for (int c = 0; c < DP; c += 2)
       qp[r][c / 2] = pack2(qr[c] * p.qscale, qr[c + 1] * p.qscale);
   }
+  cp_async_wait_all();
   __syncthreads();
 
   // ---- main loop: chunk maxima, running k+1 best chunks -------------------

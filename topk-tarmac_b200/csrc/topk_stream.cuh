@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(128) topk_stream_kernel(AttnParams p) {
 
   for (int t0 = 0; t0 < N; t0 += TK) {
     __syncthreads();
-    stage_tile<DP, TK, T>(sk, K, p.st.kn, t0, N, d, vec);
+    stage_rows<DP, T>(sk, DP, K, p.st.kn, t0, TK, N, d, vec);
+    cp_async_wait_all();
     __syncthreads();
     if (!active) continue;
     const int nk = min(TK, N - t0);
