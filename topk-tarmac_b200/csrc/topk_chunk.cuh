@@ -11,19 +11,21 @@
 //   registers as fp32 pairs) and its 4 warps split the keys into contiguous
 //   ranges of 16-key chunks.
 // * Scores use the packed fp32x2 FMA (fma.rn.f32x2): even and odd columns
-//   accumulate in the two halves and are added at the end, so the FMA pipe
-//   does 2 FMAs per issue slot and leaves slots for the selection.
+//   accumulate in the two halves and are added at the end. Two keys are
+//   scored against all QPT queries in lock-step, so 2*QPT independent FMA
+//   chains are interleaved in program order.
 // * Per query and chunk only the chunk maximum is formed (three-input max),
-//   and a branch-free running buffer keeps the k+1 best chunks (ordered by
-//   (max, chunk index) with the tie rule). The k best scores lie in the k best
-//   chunks: every chunk outside them has k chunk maxima above its own. One
-//   extra chunk covers the diagonal score, which the main loop does not mask
-//   (it can only inflate its own chunk's maximum).
+//   and a branch-free running buffer keeps the k best chunks, ordered by
+//   (maximum, chunk index) with the tie rule. The k best scores of the row lie
+//   in those k chunks: any other chunk has k chunk maxima above its own, each
+//   the maximum of a distinct score that beats all of its scores. The
+//   diagonal is masked only in the 2*QPT chunks that can hold it for this
+//   block's queries (a warp-uniform test per chunk).
 // * The warps' chunk lists are merged through shared memory; each lane then
-//   recomputes — bit-identically — the scores of its query's k+1 candidate
-//   chunks, drops the diagonal, and keeps the k best by (score, index) with
-//   the tie rule. Only scores >= the (k+1)-th chunk maximum (a lower bound of
-//   the k-th score) reach the exact buffer.
+//   recomputes — bit-identically — the scores of its query's k candidate
+//   chunks and keeps the k best by (score, index) with the tie rule. Only
+//   scores >= the k-th chunk maximum (a lower bound of the k-th score) reach
+//   the exact buffer.
 #pragma once
 
 #include "topk_stream.cuh"
@@ -59,6 +61,38 @@ __device__ __forceinline__ void ins_idx(float (&bs)[KM], int (&bi)[KM],
   }
 }
 
+// Scores of two key rows (shared memory, 16-byte aligned) against QPT query
+// rows, chains interleaved; each score is accumulated in exactly the order
+// of dot_pairs, so the final recompute reproduces it bit for bit.
+template <int DP, int QPT>
+__device__ __forceinline__ void dot2keys(const uint64_t (&qp)[QPT][DP / 2],
+                                         const float* k0, const float* k1,
+                                         float (&s0)[QPT], float (&s1)[QPT]) {
+  uint64_t a0[QPT], a1[QPT];
+#pragma unroll
+  for (int r = 0; r < QPT; ++r) a0[r] = a1[r] = 0ull;
+#pragma unroll
+  for (int c = 0; c < DP; c += 4) {
+    const ulonglong2 x = *reinterpret_cast<const ulonglong2*>(k0 + c);
+    const ulonglong2 y = *reinterpret_cast<const ulonglong2*>(k1 + c);
+#pragma unroll
+    for (int r = 0; r < QPT; ++r) {
+      a0[r] = ffma2(qp[r][c / 2], x.x, a0[r]);
+      a1[r] = ffma2(qp[r][c / 2], y.x, a1[r]);
+    }
+#pragma unroll
+    for (int r = 0; r < QPT; ++r) {
+      a0[r] = ffma2(qp[r][c / 2 + 1], x.y, a0[r]);
+      a1[r] = ffma2(qp[r][c / 2 + 1], y.y, a1[r]);
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < QPT; ++r) {
+    s0[r] = hsum2(a0[r]);
+    s1[r] = hsum2(a1[r]);
+  }
+}
+
 template <int DP>
 __host__ __device__ constexpr int chunk_row_stride() {
   return DP + 4;  // padding spreads the recompute's row gathers over banks
@@ -71,10 +105,9 @@ __host__ __device__ constexpr size_t chunk_smem_bytes(int NC) {
 }
 
 template <int DP, int QPT, int KC, bool TIE_HIGH, typename T>
-__global__ void __launch_bounds__(CH_WARPS * 32)
+__global__ void __launch_bounds__(CH_WARPS * 32, DP >= 128 ? 2 : 4)
     topk_chunk_kernel(AttnParams p, int NC) {
   constexpr int KS = chunk_row_stride<DP>();
-  constexpr int KM = KC - 1;  // exact buffer: the k best scores (k <= KM)
   extern __shared__ __align__(16) float smem[];
   float* sK = smem;
   float* lv = sK + (size_t)NC * CH * KS;          // [QPT][warps][32][KC]
@@ -115,7 +148,7 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
   cp_async_wait_all();
   __syncthreads();
 
-  // ---- main loop: chunk maxima, running k+1 best chunks -------------------
+  // ---- main loop: chunk maxima, running k best chunks --------------------
   float cbv[QPT][KC];
   int cbi[QPT][KC];
 #pragma unroll
@@ -127,31 +160,40 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
     }
   const int c0 = (warp * NC) / CH_WARPS;
   const int c1 = ((warp + 1) * NC) / CH_WARPS;
+  // chunks holding this block's diagonal: keys of queries g*32*QPT ...
+  const int diag0 = g * 2 * QPT;
   for (int c = c0; c < c1; ++c) {
     const float* kb = sK + (size_t)c * CH * KS;
     float cm[QPT];
 #pragma unroll
     for (int r = 0; r < QPT; ++r) cm[r] = -INFINITY;
-    if ((c + 1) * CH <= N) {
-#pragma unroll 4
+    const bool plain = (c + 1) * CH <= N && (c < diag0 || c >= diag0 + 2 * QPT);
+    if (plain) {
+#pragma unroll 2
       for (int jj = 0; jj < CH; jj += 2) {
+        float s0[QPT], s1[QPT];
+        dot2keys<DP, QPT>(qp, kb + jj * KS, kb + (jj + 1) * KS, s0, s1);
 #pragma unroll
-        for (int r = 0; r < QPT; ++r) {
-          const float s0 = dot_pairs<DP>(qp[r], kb + jj * KS);
-          const float s1 = dot_pairs<DP>(qp[r], kb + (jj + 1) * KS);
-          cm[r] = max3f(cm[r], s0, s1);
-        }
+        for (int r = 0; r < QPT; ++r) cm[r] = max3f(cm[r], s0[r], s1[r]);
       }
     } else {
-      const int nk = N - c * CH;  // partial last chunk
-      for (int jj = 0; jj < nk; ++jj) {
+      // partial last chunk or a diagonal chunk: keys >= N (zero rows in
+      // shared memory) and the query's own key do not count
+      for (int jj = 0; jj < CH; jj += 2) {
+        float s0[QPT], s1[QPT];
+        dot2keys<DP, QPT>(qp, kb + jj * KS, kb + (jj + 1) * KS, s0, s1);
+        const int j0 = c * CH + jj;
 #pragma unroll
-        for (int r = 0; r < QPT; ++r)
-          cm[r] = fmaxf(cm[r], dot_pairs<DP>(qp[r], kb + jj * KS));
+        for (int r = 0; r < QPT; ++r) {
+          const float a = (j0 < N && j0 != qi[r]) ? s0[r] : -INFINITY;
+          const float e = (j0 + 1 < N && j0 + 1 != qi[r]) ? s1[r] : -INFINITY;
+          cm[r] = max3f(cm[r], a, e);
+        }
       }
     }
 #pragma unroll
-    for (int r = 0; r < QPT; ++r) buf_insert<KC, TIE_HIGH>(cbv[r], cbi[r], cm[r], c);
+    for (int r = 0; r < QPT; ++r)
+      buf_insert<KC, TIE_HIGH>(cbv[r], cbi[r], cm[r], c);
   }
 
   // ---- publish each warp's chunk lists ------------------------------------
@@ -194,10 +236,10 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
     }
   }
   const float thr = mv[KC - 1];  // <= the k-th best score of the row
-  float bs[KM];
-  int bi[KM];
+  float bs[KC];
+  int bi[KC];
 #pragma unroll
-  for (int m = 0; m < KM; ++m) {
+  for (int m = 0; m < KC; ++m) {
     bs[m] = -INFINITY;
     bi[m] = -1;
   }
@@ -216,7 +258,7 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
       const int jr = (jj + lane) & (CH - 1);
       const int j = cid * CH + jr;
       const float s = dot_pairs<DP>(qf, sK + (size_t)j * KS);
-      if (jr < nk && j != i && s >= thr) ins_idx<KM, TIE_HIGH>(bs, bi, s, j);
+      if (jr < nk && j != i && s >= thr) ins_idx<KC, TIE_HIGH>(bs, bi, s, j);
     }
   }
 
@@ -224,10 +266,10 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
   const int kk = p.topk;
   const float mx = bs[0] * p.post_scale;
   float den = 0.f;
-  float e[KM];
+  float e[KC];
   bool empty = false;
 #pragma unroll
-  for (int m = 0; m < KM; ++m) {
+  for (int m = 0; m < KC; ++m) {
     e[m] = (m < kk) ? expf(bs[m] * p.post_scale - mx) : 0.f;
     den += e[m];
     empty |= (m < kk) && (bi[m] < 0);
@@ -236,7 +278,7 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
 #pragma unroll
   for (int c = 0; c < DP; ++c) acc[c] = 0.f;
 #pragma unroll
-  for (int m = 0; m < KM; ++m) {
+  for (int m = 0; m < KC; ++m) {
     if (m < kk && !empty) {
       const float w = e[m] / den;
       const T* vr = V + (int64_t)bi[m] * p.st.vn;
@@ -268,7 +310,7 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
   if (p.idx_out != nullptr) {
     int32_t* io = p.idx_out + ((int64_t)b * N + i) * kk;
 #pragma unroll
-    for (int m = 0; m < KM; ++m)
+    for (int m = 0; m < KC; ++m)
       if (m < kk) io[m] = bi[m];
   }
 }
@@ -277,14 +319,15 @@ __global__ void __launch_bounds__(CH_WARPS * 32)
 // slots must stay within the register budget.
 template <int DP, int KC>
 constexpr int chunk_qpt() {
-  return DP >= 64 ? 1 : (DP >= 32 ? (KC >= 9 ? 1 : 2) : (KC >= 9 ? 2 : 4));
+  return DP >= 64 ? 1 : (DP >= 32 ? (KC >= 8 ? 1 : 2) : (KC >= 8 ? 2 : 4));
 }
 
 // Largest dynamic shared memory the chunked kernel may take per block.
 constexpr size_t CHUNK_SMEM_MAX = 200 * 1024;
 
+// chunk slots: the k-bucket {1, 2, 4, 8} holding k
 constexpr int chunk_slots(int topk) {
-  return topk <= 1 ? 2 : (topk <= 2 ? 3 : (topk <= 4 ? 5 : 9));
+  return topk <= 1 ? 1 : (topk <= 2 ? 2 : (topk <= 4 ? 4 : 8));
 }
 
 template <int DP, int KC>
@@ -295,10 +338,10 @@ size_t chunk_smem_for(int N) {
 template <int DP>
 size_t chunk_smem_dp(int N, int topk) {
   switch (chunk_slots(topk)) {
+    case 1: return chunk_smem_for<DP, 1>(N);
     case 2: return chunk_smem_for<DP, 2>(N);
-    case 3: return chunk_smem_for<DP, 3>(N);
-    case 5: return chunk_smem_for<DP, 5>(N);
-    default: return chunk_smem_for<DP, 9>(N);
+    case 4: return chunk_smem_for<DP, 4>(N);
+    default: return chunk_smem_for<DP, 8>(N);
   }
 }
 
@@ -331,10 +374,10 @@ cudaError_t launch_chunk_t(const AttnParams& p, cudaStream_t s) {
 template <int DP, bool TIE_HIGH, typename T>
 cudaError_t launch_chunk_kc(const AttnParams& p, cudaStream_t s) {
   switch (chunk_slots(p.topk)) {
+    case 1: return launch_chunk_t<DP, 1, TIE_HIGH, T>(p, s);
     case 2: return launch_chunk_t<DP, 2, TIE_HIGH, T>(p, s);
-    case 3: return launch_chunk_t<DP, 3, TIE_HIGH, T>(p, s);
-    case 5: return launch_chunk_t<DP, 5, TIE_HIGH, T>(p, s);
-    default: return launch_chunk_t<DP, 9, TIE_HIGH, T>(p, s);
+    case 4: return launch_chunk_t<DP, 4, TIE_HIGH, T>(p, s);
+    default: return launch_chunk_t<DP, 8, TIE_HIGH, T>(p, s);
   }
 }
 
