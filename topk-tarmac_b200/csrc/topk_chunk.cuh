@@ -9,7 +9,7 @@
 // * The episode's K rows are staged once into shared memory (fp32, rows padded
 //   to DP+4 floats). A block owns 32*QPT queries (QPT per lane, q in
 //   registers as fp32 pairs) and its 4 warps split the keys into contiguous
-//   ranges of 16-key chunks.
+//   ranges of CH-key chunks (CH = 4, 8 or 16 for k <= 2, 4, 8).
 // * Scores use the packed fp32x2 FMA (fma.rn.f32x2): even and odd columns
 //   accumulate in the two halves and are added at the end. Two keys are
 //   scored against all QPT queries in lock-step, so 2*QPT independent FMA
@@ -19,8 +19,8 @@
 //   (maximum, chunk index) with the tie rule. The k best scores of the row lie
 //   in those k chunks: any other chunk has k chunk maxima above its own, each
 //   the maximum of a distinct score that beats all of its scores. The
-//   diagonal is masked only in the 2*QPT chunks that can hold it for this
-//   block's queries (a warp-uniform test per chunk).
+//   diagonal is masked only in the chunks that can hold it for this block's
+//   queries (a warp-uniform test per chunk).
 // * The warps' chunk lists are merged through shared memory; each lane then
 //   recomputes — bit-identically — the scores of its query's k candidate
 //   chunks and keeps the k best by (score, index) with the tie rule. Only
@@ -32,7 +32,6 @@
 
 namespace tarmac {
 
-constexpr int CH = 16;       // keys per chunk
 constexpr int CH_WARPS = 4;  // warps per block (they split the keys)
 
 // (a, ia) precedes (b, ib) in the retained order: score descending, ties by
@@ -98,13 +97,13 @@ __host__ __device__ constexpr int chunk_row_stride() {
   return DP + 4;  // padding spreads the recompute's row gathers over banks
 }
 
-template <int DP, int QPT, int KC>
+template <int DP, int QPT, int KC, int CH>
 __host__ __device__ constexpr size_t chunk_smem_bytes(int NC) {
   return (size_t)NC * CH * chunk_row_stride<DP>() * 4 +
          (size_t)QPT * CH_WARPS * 32 * KC * 8;
 }
 
-template <int DP, int QPT, int KC, bool TIE_HIGH, typename T>
+template <int DP, int QPT, int KC, int CH, bool TIE_HIGH, typename T>
 __global__ void __launch_bounds__(CH_WARPS * 32, DP >= 128 ? 2 : 4)
     topk_chunk_kernel(AttnParams p, int NC) {
   constexpr int KS = chunk_row_stride<DP>();
@@ -160,16 +159,17 @@ __global__ void __launch_bounds__(CH_WARPS * 32, DP >= 128 ? 2 : 4)
     }
   const int c0 = (warp * NC) / CH_WARPS;
   const int c1 = ((warp + 1) * NC) / CH_WARPS;
-  // chunks holding this block's diagonal: keys of queries g*32*QPT ...
-  const int diag0 = g * 2 * QPT;
+  // chunks holding this block's diagonal (keys g*32*QPT ... +32*QPT-1)
+  const int diag0 = (g * 32 * QPT) / CH;
+  const int diag1 = (g * 32 * QPT + 32 * QPT + CH - 1) / CH;
   for (int c = c0; c < c1; ++c) {
     const float* kb = sK + (size_t)c * CH * KS;
     float cm[QPT];
 #pragma unroll
     for (int r = 0; r < QPT; ++r) cm[r] = -INFINITY;
-    const bool plain = (c + 1) * CH <= N && (c < diag0 || c >= diag0 + 2 * QPT);
+    const bool plain = (c + 1) * CH <= N && (c < diag0 || c >= diag1);
     if (plain) {
-#pragma unroll 2
+#pragma unroll
       for (int jj = 0; jj < CH; jj += 2) {
         float s0[QPT], s1[QPT];
         dot2keys<DP, QPT>(qp, kb + jj * KS, kb + (jj + 1) * KS, s0, s1);
@@ -322,6 +322,11 @@ constexpr int chunk_qpt() {
   return DP >= 64 ? 1 : (DP >= 32 ? (KC >= 8 ? 1 : 2) : (KC >= 8 ? 2 : 4));
 }
 
+// Keys per chunk for KC chunk slots: short chunks keep the final recompute
+// (KC * CH scores per query) small; the per-chunk buffer update (about 4 KC
+// instructions per query) must stay well below the chunk's FMA-pipe time.
+constexpr int chunk_len(int KC) { return KC <= 2 ? 4 : (KC <= 4 ? 8 : 16); }
+
 // Largest dynamic shared memory the chunked kernel may take per block.
 constexpr size_t CHUNK_SMEM_MAX = 200 * 1024;
 
@@ -332,7 +337,8 @@ constexpr int chunk_slots(int topk) {
 
 template <int DP, int KC>
 size_t chunk_smem_for(int N) {
-  return chunk_smem_bytes<DP, chunk_qpt<DP, KC>(), KC>(cdiv(N, CH));
+  constexpr int CH = chunk_len(KC);
+  return chunk_smem_bytes<DP, chunk_qpt<DP, KC>(), KC, CH>(cdiv(N, CH));
 }
 
 template <int DP>
@@ -358,15 +364,16 @@ inline bool chunk_fits(int N, int d, int topk) {
 template <int DP, int KC, bool TIE_HIGH, typename T>
 cudaError_t launch_chunk_t(const AttnParams& p, cudaStream_t s) {
   constexpr int QPT = chunk_qpt<DP, KC>();
+  constexpr int CH = chunk_len(KC);
   const int NC = cdiv(p.N, CH);
-  const size_t sm = chunk_smem_bytes<DP, QPT, KC>(NC);
+  const size_t sm = chunk_smem_bytes<DP, QPT, KC, CH>(NC);
   cudaError_t e = cudaFuncSetAttribute(
-      topk_chunk_kernel<DP, QPT, KC, TIE_HIGH, T>,
+      topk_chunk_kernel<DP, QPT, KC, CH, TIE_HIGH, T>,
       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
   if (e != cudaSuccess) return e;
   const int64_t blocks = (int64_t)p.B * cdiv(p.N, 32 * QPT);
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  topk_chunk_kernel<DP, QPT, KC, TIE_HIGH, T>
+  topk_chunk_kernel<DP, QPT, KC, CH, TIE_HIGH, T>
       <<<(unsigned)blocks, CH_WARPS * 32, sm, s>>>(p, NC);
   return cudaGetLastError();
 }
