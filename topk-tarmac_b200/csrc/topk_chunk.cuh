@@ -8,11 +8,12 @@
 //
 // * The episode's K rows are staged once into shared memory (fp32, rows padded
 //   to DP+4 floats). A block owns 32*QPT queries (QPT per lane, q in
-//   registers) and its 4 warps split the keys into contiguous ranges of
-//   CH-key chunks (CH = 4, 8 or 16 for k <= 2, 4, 8).
-// * Two keys, read with broadcast loads, are scored against all QPT queries
-//   in lock-step, so 2*QPT independent fp32 FMA chains are interleaved in
-//   program order.
+//   registers as fp32 pairs) and its 4 warps split the keys into contiguous
+//   ranges of CH-key chunks (CH = 4, 8 or 16 for k <= 2, 4, 8).
+// * Scores use the packed fp32x2 FMA (fma.rn.f32x2): even and odd columns
+//   accumulate in the two halves and are added at the end. Two keys are
+//   scored against all QPT queries in lock-step, so 2*QPT independent FMA
+//   chains are interleaved in program order.
 // * Per query and chunk only the chunk maximum is formed (three-input max),
 //   and a branch-free running buffer keeps the k best chunks, ordered by
 //   (maximum, chunk index) with the tie rule. The k best scores of the row lie
@@ -59,58 +60,35 @@ __device__ __forceinline__ void ins_idx(float (&bs)[KM], int (&bi)[KM],
   }
 }
 
-// Score of one query row (registers) against one key row (shared memory,
-// 16-byte aligned): a single fp32 FMA chain over the columns in order. The
-// main loop (dot2keys) and the final recompute both form every score in this
-// order, so a recomputed score is bit-identical.
-template <int DP>
-__device__ __forceinline__ float dot_row(const float (&q)[DP], const float* kr) {
-  float s = 0.f;
-#pragma unroll
-  for (int c = 0; c < DP; c += 4) {
-    const float4 k = *reinterpret_cast<const float4*>(kr + c);
-    s = fmaf(q[c], k.x, s);
-    s = fmaf(q[c + 1], k.y, s);
-    s = fmaf(q[c + 2], k.z, s);
-    s = fmaf(q[c + 3], k.w, s);
-  }
-  return s;
-}
-
-// Scores of two key rows against QPT query rows, the 2*QPT FMA chains
-// interleaved column by column (each chain in dot_row's order). Scalar FFMA:
-// in this operand pattern (three distinct operands per FMA) it sustained more
-// throughput on B200 than the packed fp32x2 FMA.
+// Scores of two key rows (shared memory, 16-byte aligned) against QPT query
+// rows, chains interleaved; each score is accumulated in exactly the order
+// of dot_pairs, so the final recompute reproduces it bit for bit.
 template <int DP, int QPT>
-__device__ __forceinline__ void dot2keys(const float (&q)[QPT][DP],
+__device__ __forceinline__ void dot2keys(const uint64_t (&qp)[QPT][DP / 2],
                                          const float* k0, const float* k1,
                                          float (&s0)[QPT], float (&s1)[QPT]) {
+  uint64_t a0[QPT], a1[QPT];
 #pragma unroll
-  for (int r = 0; r < QPT; ++r) s0[r] = s1[r] = 0.f;
+  for (int r = 0; r < QPT; ++r) a0[r] = a1[r] = 0ull;
 #pragma unroll
   for (int c = 0; c < DP; c += 4) {
-    const float4 x = *reinterpret_cast<const float4*>(k0 + c);
-    const float4 y = *reinterpret_cast<const float4*>(k1 + c);
+    const ulonglong2 x = *reinterpret_cast<const ulonglong2*>(k0 + c);
+    const ulonglong2 y = *reinterpret_cast<const ulonglong2*>(k1 + c);
 #pragma unroll
     for (int r = 0; r < QPT; ++r) {
-      s0[r] = fmaf(q[r][c], x.x, s0[r]);
-      s1[r] = fmaf(q[r][c], y.x, s1[r]);
+      a0[r] = ffma2(qp[r][c / 2], x.x, a0[r]);
+      a1[r] = ffma2(qp[r][c / 2], y.x, a1[r]);
     }
 #pragma unroll
     for (int r = 0; r < QPT; ++r) {
-      s0[r] = fmaf(q[r][c + 1], x.y, s0[r]);
-      s1[r] = fmaf(q[r][c + 1], y.y, s1[r]);
+      a0[r] = ffma2(qp[r][c / 2 + 1], x.y, a0[r]);
+      a1[r] = ffma2(qp[r][c / 2 + 1], y.y, a1[r]);
     }
+  }
 #pragma unroll
-    for (int r = 0; r < QPT; ++r) {
-      s0[r] = fmaf(q[r][c + 2], x.z, s0[r]);
-      s1[r] = fmaf(q[r][c + 2], y.z, s1[r]);
-    }
-#pragma unroll
-    for (int r = 0; r < QPT; ++r) {
-      s0[r] = fmaf(q[r][c + 3], x.w, s0[r]);
-      s1[r] = fmaf(q[r][c + 3], y.w, s1[r]);
-    }
+  for (int r = 0; r < QPT; ++r) {
+    s0[r] = hsum2(a0[r]);
+    s1[r] = hsum2(a1[r]);
   }
 }
 
@@ -149,20 +127,22 @@ __global__ void __launch_bounds__(CH_WARPS * 32, DP >= 128 ? 2 : 4)
   // ---- stage the episode's keys: rows [0, NC*CH), zero beyond N and d ----
   stage_rows<DP, T>(sK, KS, K, p.st.kn, 0, NC * CH, N, d, vec);
 
-  // ---- queries (power-of-two scale folded in exactly) ---------------------
-  float qp[QPT][DP];
+  // ---- queries as column pairs -------------------------------------------
+  uint64_t qp[QPT][DP / 2];
   int qi[QPT];
 #pragma unroll
   for (int r = 0; r < QPT; ++r) {
     qi[r] = g * 32 * QPT + r * 32 + lane;
+    float qr[DP];
     if (qi[r] < N) {
-      load_row<DP, T>(qp[r], Q + (int64_t)qi[r] * p.st.qn, d, vec);
+      load_row<DP, T>(qr, Q + (int64_t)qi[r] * p.st.qn, d, vec);
     } else {
 #pragma unroll
-      for (int c = 0; c < DP; ++c) qp[r][c] = 0.f;
+      for (int c = 0; c < DP; ++c) qr[c] = 0.f;
     }
 #pragma unroll
-    for (int c = 0; c < DP; ++c) qp[r][c] *= p.qscale;
+    for (int c = 0; c < DP; c += 2)
+      qp[r][c / 2] = pack2(qr[c] * p.qscale, qr[c + 1] * p.qscale);
   }
   cp_async_wait_all();
   __syncthreads();
@@ -232,10 +212,14 @@ __global__ void __launch_bounds__(CH_WARPS * 32, DP >= 128 ? 2 : 4)
   const int r = warp;
   const int i = g * 32 * QPT + r * 32 + lane;
   if (i >= N) return;
-  float qf[DP];
-  load_row<DP, T>(qf, Q + (int64_t)i * p.st.qn, d, vec);
+  uint64_t qf[DP / 2];
+  {
+    float qr[DP];
+    load_row<DP, T>(qr, Q + (int64_t)i * p.st.qn, d, vec);
 #pragma unroll
-  for (int c = 0; c < DP; ++c) qf[c] *= p.qscale;
+    for (int c = 0; c < DP; c += 2)
+      qf[c / 2] = pack2(qr[c] * p.qscale, qr[c + 1] * p.qscale);
+  }
   float mv[KC];
   int mi[KC];
 #pragma unroll
@@ -273,7 +257,7 @@ __global__ void __launch_bounds__(CH_WARPS * 32, DP >= 128 ? 2 : 4)
     for (int jj = 0; jj < CH; ++jj) {
       const int jr = (jj + lane) & (CH - 1);
       const int j = cid * CH + jr;
-      const float s = dot_row<DP>(qf, sK + (size_t)j * KS);
+      const float s = dot_pairs<DP>(qf, sK + (size_t)j * KS);
       if (jr < nk && j != i && s >= thr) ins_idx<KC, TIE_HIGH>(bs, bi, s, j);
     }
   }
