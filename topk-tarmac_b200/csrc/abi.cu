@@ -6,7 +6,7 @@
 #include <math.h>
 
 #include "common.cuh"
-#include "topk_pair.cuh"
+#include "topk_chunk.cuh"
 
 namespace tarmac {
 cudaError_t launch_topk_stream_f32(const AttnParams& p, bool tie_high,
@@ -22,7 +22,7 @@ cudaError_t launch_topk_chunk_bf16_high(const AttnParams& p, cudaStream_t s);
 // the episode's keys fit its shared memory, else the streaming kernel.
 static cudaError_t launch_topk_small_k(const AttnParams& p, int dtype,
                                        bool tie_high, cudaStream_t s) {
-  if (resident_fits(p.N, p.d, p.topk)) {
+  if (chunk_fits(p.N, p.d, p.topk)) {
     if (dtype == TARMAC_BF16)
       return tie_high ? launch_topk_chunk_bf16_high(p, s)
                       : launch_topk_chunk_bf16_low(p, s);

@@ -388,4 +388,13 @@ cudaError_t launch_chunk_kc(const AttnParams& p, cudaStream_t s) {
   }
 }
 
+// One element type and tie rule per translation unit (compile in parallel).
+template <bool TIE_HIGH, typename T>
+cudaError_t launch_chunk_dt(const AttnParams& p, cudaStream_t s) {
+  if (p.d <= 16) return launch_chunk_kc<16, TIE_HIGH, T>(p, s);
+  if (p.d <= 32) return launch_chunk_kc<32, TIE_HIGH, T>(p, s);
+  if (p.d <= 64) return launch_chunk_kc<64, TIE_HIGH, T>(p, s);
+  return launch_chunk_kc<128, TIE_HIGH, T>(p, s);
+}
+
 }  // namespace tarmac

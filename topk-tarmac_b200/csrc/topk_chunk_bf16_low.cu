@@ -1,9 +1,9 @@
 // topk_chunk_bf16_low.cu — chunked top-k kernel instantiations: bf16 inputs,
 // lowest index wins a tie at the k-th score.
-#include "topk_pair.cuh"
+#include "topk_chunk.cuh"
 
 namespace tarmac {
 cudaError_t launch_topk_chunk_bf16_low(const AttnParams& p, cudaStream_t s) {
-  return launch_resident_dt<false, __nv_bfloat16>(p, s);
+  return launch_chunk_dt<false, __nv_bfloat16>(p, s);
 }
 }  // namespace tarmac
