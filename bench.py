@@ -48,6 +48,17 @@ def log(*a) -> None:
     print(*a, file=sys.stderr, flush=True)
 
 
+def _profiled_traffic() -> float | None:
+    """DRAM bytes (read + write) of one top-k launch at this workload, from the
+    committed ncu summary (line ``traffic_bytes_per_launch: N``)."""
+    f = REPO / "profiles" / "topk_chunk_c2.md"
+    if not f.exists():
+        return None
+    import re
+    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
 def _peaks() -> dict:
     f = REPO / "MEASURED_PEAKS.json"
     if f.exists():
@@ -391,7 +402,9 @@ def run_ours(args) -> int:
         "roofline": {"bound": "hbm", "achieved": achieved_gbs,
                      "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": achieved_gbs / peaks["hbm_gbs"],
-                     "traffic": args.traffic, "peak_src": peaks["src"]},
+                     "traffic": (args.traffic if args.traffic is not None
+                                 else _profiled_traffic()),
+                     "peak_src": peaks["src"]},
         "roofline_compute": {"bound": "fp32_ffma", "achieved": achieved_tf,
                              "peak": fp32_tf, "unit": "TFLOP/s",
                              "frac": achieved_tf / fp32_tf if fp32_tf else None,
