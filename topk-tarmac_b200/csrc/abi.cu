@@ -18,10 +18,17 @@ cudaError_t launch_topk_chunk_f32_high(const AttnParams& p, cudaStream_t s);
 cudaError_t launch_topk_chunk_bf16_low(const AttnParams& p, cudaStream_t s);
 cudaError_t launch_topk_chunk_bf16_high(const AttnParams& p, cudaStream_t s);
 
-// k <= 8 with the lowest- or highest-index tie rule: the chunked kernel when
-// the episode's keys fit its shared memory, else the streaming kernel.
+bool topk_tc_supported(const AttnParams& p);
+cudaError_t launch_topk_tc(const AttnParams& p, bool tie_high, cudaStream_t s);
+
+// k <= 8 with the lowest- or highest-index tie rule: bf16 episodes of 128 to
+// 512 agents form their scores on the tensor cores; otherwise the chunked
+// FFMA kernel when the episode's keys fit its shared memory, else the
+// streaming kernel.
 static cudaError_t launch_topk_small_k(const AttnParams& p, int dtype,
                                        bool tie_high, cudaStream_t s) {
+  if (dtype == TARMAC_BF16 && topk_tc_supported(p))
+    return launch_topk_tc(p, tie_high, s);
   if (chunk_fits(p.N, p.d, p.topk)) {
     if (dtype == TARMAC_BF16)
       return tie_high ? launch_topk_chunk_bf16_high(p, s)

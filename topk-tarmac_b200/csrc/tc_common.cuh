@@ -1,0 +1,216 @@
+// tc_common.cuh — fifth-generation tensor core (tcgen05) helpers for sm_100a.
+//
+// Operand layout: bf16 tiles in shared memory in the no-swizzle, K-major
+// core-matrix layout. A core matrix is 8 rows x 16 bytes (8 bf16 along K),
+// stored contiguously (128 B). For a [rows x DP] tile with KC = DP/8 16-byte
+// chunks per row, element (r, k) sits at byte
+//     ((r / 8) * KC + k / 8) * 128 + (r % 8) * 16 + (k % 8) * 2,
+// so the descriptor's leading-dimension byte offset (next K chunk) is 128 and
+// its stride-dimension byte offset (next 8 rows) is KC * 128. One MMA
+// instruction consumes K = 16 (two chunks); K step s starts 2*s*128 bytes in.
+//
+// For an operand whose contiguous dimension is M/N (MN-major, e.g. V as the B
+// operand of P.V, contiguous along d): element (k, n) sits at byte
+//     ((k / 8) + (n / 8) * (KROWS / 8)) * 128 + (k % 8) * 16 + (n % 8) * 2,
+// i.e. core matrices of 8 K-rows x 8 N-values; leading-dimension offset
+// (next 8 K rows) 128 B, stride-dimension offset (next 8 N values)
+// KROWS/8 * 128 B.
+//
+// Accumulators live in tensor memory (TMEM): an M=128 tile puts row m in TMEM
+// lane m and column n in TMEM column base+n; warp w of the block reads lanes
+// 32*(w%4) .. 32*(w%4)+31.
+#pragma once
+
+#include "common.cuh"
+
+namespace tarmac {
+namespace tc {
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// shared-memory matrix descriptor, no swizzle
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo,
+                                              uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for sm_100
+  return d;                // base offset 0, absolute LBO mode, SWIZZLE_NONE
+}
+
+// instruction descriptor: bf16 x bf16 -> fp32, M x N, A/B majorness
+__host__ __device__ constexpr uint32_t idesc_bf16(int m, int n, bool a_mn,
+                                                  bool b_mn) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) |
+         ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(n >> 3) << 17) |
+         ((uint32_t)(m >> 4) << 24);
+}
+
+// D[tmem] (+)= A * B, issued by one thread
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t adesc,
+                                         uint64_t bdesc, uint32_t idesc,
+                                         bool accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate));
+}
+
+// arrive on an mbarrier when all MMAs issued so far by this thread complete
+__device__ __forceinline__ void mma_commit(uint64_t* mbar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 "
+      "[%0];" ::"r"(smem_addr(mbar))
+      : "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* mbar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(mbar)),
+               "r"(count));
+}
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// Wait for the mbarrier phase `parity` to complete, polling at most
+// `limit` times. Returns false if the limit ran out.
+__device__ __forceinline__ bool mbar_wait(uint64_t* mbar, uint32_t parity,
+                                          uint32_t limit = (1u << 24)) {
+  const uint32_t a = smem_addr(mbar);
+  for (uint32_t it = 0; it < limit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], "
+        "%2;\nselp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// TMEM allocation by one full warp; the base address is written to *dst.
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+          smem_addr(dst)),
+      "r"(ncols));
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t base, uint32_t ncols) {
+  asm volatile(
+      "tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(base),
+      "r"(ncols));
+}
+
+__device__ __forceinline__ void fence_before_sync() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after_sync() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+// generic-proxy shared-memory writes -> visible to the tensor core
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 32 consecutive fp32 columns of this thread's TMEM lane (warp-collective).
+// The load and its wait sit in one asm statement, so no use of the outputs
+// can be scheduled ahead of the wait.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+        "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]),
+        "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// 8 consecutive fp32 columns of this thread's TMEM lane (warp-collective).
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float (&v)[8]) {
+  uint32_t r[8];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];\n"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]),
+        "=r"(r[6]), "=r"(r[7])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = __uint_as_float(r[j]);
+}
+
+// 8 consecutive fp32 columns into this thread's TMEM lane (warp-collective);
+// the store is complete (visible to later tcgen05 operations of this thread
+// after a fence) when the call returns.
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};\n"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])),
+      "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7]))
+      : "memory");
+}
+
+// byte offset of row r, 16-byte chunk c in a K-major core-matrix tile with
+// KC chunks per row
+__device__ __forceinline__ uint32_t kmajor_off(int r, int c, int KC) {
+  return (uint32_t)(((r >> 3) * KC + c) * 128 + (r & 7) * 16);
+}
+
+// Stage rows [r0, r0 + nrows) of a [*, d] bf16 matrix (row stride rs
+// elements) into a K-major core-matrix tile of DP columns, zero-filling rows
+// >= rlimit and columns >= d. 16-byte cp.async when `vec` (d % 8 == 0 and
+// 16-byte aligned rows); element copies otherwise. All threads take part;
+// the caller waits with cp_async_wait_all().
+template <int DP>
+__device__ __forceinline__ void stage_kmajor(unsigned char* tile,
+                                             const __nv_bfloat16* src,
+                                             int64_t rs, int r0, int nrows,
+                                             int rlimit, int d, bool vec) {
+  constexpr int KC = DP / 8;
+  const uint32_t base = smem_addr(tile);
+  for (int e = threadIdx.x; e < nrows * KC; e += blockDim.x) {
+    const int r = e / KC, c = e - (e / KC) * KC;
+    const uint32_t off = kmajor_off(r, c, KC);
+    const int gr = r0 + r;
+    const int c0 = c * 8;
+    if (gr < rlimit && c0 < d) {
+      const __nv_bfloat16* g = src + (int64_t)gr * rs + c0;
+      if (vec) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(base + off),
+                     "l"(g)
+                     : "memory");
+      } else {
+        __nv_bfloat16 t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          t[u] = (c0 + u < d) ? g[u] : __float2bfloat16_rn(0.f);
+        *reinterpret_cast<uint4*>(tile + off) = *reinterpret_cast<uint4*>(t);
+      }
+    } else {
+      *reinterpret_cast<uint4*>(tile + off) = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+}  // namespace tc
+}  // namespace tarmac

@@ -1,0 +1,240 @@
+// topk_tc.cu — fused top-k attention for bf16 inputs with the score matrix
+// formed on the fifth-generation tensor cores (tcgen05, TMEM accumulators).
+//
+// Same function as the other fused top-k kernels (reference:
+// src/kernels/fused_topk_attention.py:211-289, 405-504 and
+// src/kernels/streaming_topk_attention.py:66-179): scores q.k with the
+// diagonal excluded, the k best kept under the lowest- or highest-index tie
+// rule, softmax over them, weighted sum of their V rows. bf16 x bf16 products
+// accumulate in fp32, the reference's "bf16 with fp32 accumulation".
+//
+// One block (4 warps) owns 128 queries of one episode; thread t of warp w
+// owns query row 32*w + t, which is also its tensor-memory (TMEM) lane.
+// * Q (128 x d) is staged once in shared memory as bf16 in the K-major
+//   core-matrix layout (tc_common.cuh); K streams through a two-slot ring of
+//   128-key tiles with 16-byte cp.async, the next tile loading while the
+//   current one is scored.
+// * Per 128-key round one thread issues tcgen05.mma (M = 128, N <= 128,
+//   K = 16 per instruction) for the 128 x 128 score tile into 128 TMEM
+//   columns and commits it to an mbarrier; a block holds 128 columns, so four
+//   blocks share an SM's TMEM and overlap each other's load, MMA and scan.
+// * Every thread scans its row's scores (tcgen05.ld, 32 columns at a time)
+//   in increasing key order and keeps the exact k best in a sorted register
+//   list: later keys enter only if they beat the last entry (strictly for the
+//   lowest-index rule, or on ties for the highest-index rule). A warp vote per
+//   key skips the insertion wherever no lane needs it. Masked keys (the
+//   diagonal, the padding beyond N) read as NaN, which beats nothing.
+// * Softmax over the k retained scores, weighted sum of their V rows
+//   gathered from global memory, store.
+#include "tc_common.cuh"
+#include "topk_chunk.cuh"
+
+namespace tarmac {
+
+constexpr int TC_THREADS = 128;
+constexpr int TC_TILE = 128;          // keys per round
+constexpr int TC_MIN_SMEM = 50 << 10; // caps residency at 4 blocks per SM
+
+template <int DP, int KC, bool TIE_HIGH>
+__global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
+    topk_tc_kernel(AttnParams p, int vec16) {
+  using T = __nv_bfloat16;
+  constexpr int KCH = DP / 8;  // 16-byte chunks per row
+  constexpr int TILE_BYTES = TC_TILE * DP * 2;
+  extern __shared__ __align__(1024) unsigned char tc_smem[];
+  unsigned char* sQ = tc_smem;                  // 128 x DP bf16
+  unsigned char* sK = sQ + TILE_BYTES;          // 2 slots of 128 x DP bf16
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ uint32_t tmem_sh;
+
+  const int N = p.N, d = p.d;
+  const int qblocks = cdiv(N, 128);
+  const int b = blockIdx.x / qblocks;
+  const int q0 = (blockIdx.x - b * qblocks) * 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = warp * 32 + lane;  // TMEM lane
+  const int i = q0 + row;            // query index
+  const bool vec = p.vec != 0;
+
+  const T* Q = static_cast<const T*>(p.q) + (int64_t)b * p.st.qb;
+  const T* K = static_cast<const T*>(p.k) + (int64_t)b * p.st.kb;
+  const T* V = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
+  T* O = static_cast<T*>(p.o) + (int64_t)b * p.st.ob;
+
+  tc::stage_kmajor<DP>(sQ, Q, p.st.qn, q0, 128, N, d, vec16 != 0);
+  tc::stage_kmajor<DP>(sK, K, p.st.kn, 0, TC_TILE, N, d, vec16 != 0);
+  if (warp == 0) tc::tmem_alloc(&tmem_sh, TC_TILE);
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&mbar, 1);
+    tc::mbar_init_fence();
+  }
+
+  // padding rows (i >= N) start full of +inf entries and so insert nothing
+  float bs[KC];
+  int bi[KC];
+#pragma unroll
+  for (int m = 0; m < KC; ++m) {
+    bs[m] = i < N ? -INFINITY : INFINITY;
+    bi[m] = -1;
+  }
+
+  const int rounds = cdiv(N, TC_TILE);
+  const uint32_t qa = tc::smem_addr(sQ), ka = tc::smem_addr(sK);
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const float qnan = __int_as_float(0x7fc00000);
+  bool ok = true;
+  uint32_t tmem = 0;
+  for (int r = 0; r < rounds; ++r) {
+    // K tile r is in its slot; every lane has finished reading round r - 1's
+    // scores from TMEM.
+    cp_async_wait_all();
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (r == 0) tmem = tmem_sh;
+    const int k0 = r * TC_TILE;
+    const int nt = min(TC_TILE, cdiv(N - k0, 32) * 32);  // columns this round
+    if (threadIdx.x == 0) {
+      const uint32_t kt = ka + (uint32_t)((r & 1) * TILE_BYTES);
+      const uint32_t idesc = tc::idesc_bf16(128, nt, false, false);
+#pragma unroll
+      for (int ks = 0; ks < DP / 16; ++ks) {
+        const uint64_t ad = tc::smem_desc(qa + ks * 256, 128, KCH * 128);
+        const uint64_t bd = tc::smem_desc(kt + ks * 256, 128, KCH * 128);
+        tc::mma_bf16(tmem, ad, bd, idesc, ks > 0);
+      }
+      tc::mma_commit(&mbar);
+    }
+    // the other slot's last reader (round r - 1's MMA) has completed
+    if (r + 1 < rounds)
+      tc::stage_kmajor<DP>(sK + ((r + 1) & 1) * TILE_BYTES, K, p.st.kn,
+                           k0 + TC_TILE, TC_TILE, N, d, vec16 != 0);
+    ok &= tc::mbar_wait(&mbar, (uint32_t)(r & 1));
+    tc::fence_after_sync();
+
+    for (int c = 0; c < nt / 32; ++c) {
+      float v[32];
+      tc::tmem_ld32(tmem + lane_off + c * 32, v);
+      const int j0 = k0 + c * 32;
+      // warp-uniform: this chunk holds the warp's diagonal or the padding
+      if (j0 + 32 > N || j0 == q0 + warp * 32) {
+#pragma unroll
+        for (int t = 0; t < 32; ++t)
+          if (j0 + t >= N || j0 + t == i) v[t] = qnan;
+      }
+#pragma unroll
+      for (int t = 0; t < 32; ++t) {
+        const bool hit = beats<TIE_HIGH>(v[t], bs[KC - 1]);
+        if (__any_sync(0xffffffffu, hit)) {
+          if (hit) buf_insert<KC, TIE_HIGH>(bs, bi, v[t], j0 + t);
+        }
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, TC_TILE);
+  if (i >= N) return;
+
+  // ---- softmax over the k retained scores, V gather-aggregate -------------
+  const int kk = p.topk;
+  const float sc = p.qscale * p.post_scale;
+  const float mx = bs[0] * sc;
+  float den = 0.f;
+  float e[KC];
+  bool empty = !ok;
+#pragma unroll
+  for (int m = 0; m < KC; ++m) {
+    e[m] = (m < kk) ? expf(bs[m] * sc - mx) : 0.f;
+    den += e[m];
+    empty |= (m < kk) && (bi[m] < 0);
+  }
+  float acc[DP];
+#pragma unroll
+  for (int c = 0; c < DP; ++c) acc[c] = 0.f;
+#pragma unroll
+  for (int m = 0; m < KC; ++m) {
+    if (m < kk && !empty) {
+      const float w = e[m] / den;
+      const T* vr = V + (int64_t)bi[m] * p.st.vn;
+#pragma unroll
+      for (int c = 0; c < DP; c += 4) {
+        if (c < d) {
+          float4 f;
+          if (vec) {
+            f = load4(vr + c);
+          } else {
+            f.x = to_f32<T>(vr[c]);
+            f.y = (c + 1 < d) ? to_f32<T>(vr[c + 1]) : 0.f;
+            f.z = (c + 2 < d) ? to_f32<T>(vr[c + 2]) : 0.f;
+            f.w = (c + 3 < d) ? to_f32<T>(vr[c + 3]) : 0.f;
+          }
+          acc[c] = fmaf(w, f.x, acc[c]);
+          acc[c + 1] = fmaf(w, f.y, acc[c + 1]);
+          acc[c + 2] = fmaf(w, f.z, acc[c + 2]);
+          acc[c + 3] = fmaf(w, f.w, acc[c + 3]);
+        }
+      }
+    }
+  }
+  if (empty) {
+#pragma unroll
+    for (int c = 0; c < DP; ++c) acc[c] = qnan;
+  }
+  store_row<DP, T>(O + (int64_t)i * p.st.on, acc, d, vec);
+  if (p.idx_out != nullptr) {
+    int32_t* io = p.idx_out + ((int64_t)b * N + i) * kk;
+#pragma unroll
+    for (int m = 0; m < KC; ++m)
+      if (m < kk) io[m] = empty ? -1 : bi[m];
+  }
+}
+
+template <int DP, int KC, bool TIE_HIGH>
+static cudaError_t launch_tc_t(const AttnParams& p, int vec16, cudaStream_t s) {
+  const size_t need = (size_t)3 * TC_TILE * DP * 2;
+  const size_t sm = need > (size_t)TC_MIN_SMEM ? need : (size_t)TC_MIN_SMEM;
+  cudaError_t e = cudaFuncSetAttribute(topk_tc_kernel<DP, KC, TIE_HIGH>,
+                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sm);
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = (int64_t)p.B * cdiv(p.N, 128);
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  topk_tc_kernel<DP, KC, TIE_HIGH>
+      <<<(unsigned)blocks, TC_THREADS, sm, s>>>(p, vec16);
+  return cudaGetLastError();
+}
+
+template <int DP, bool TIE_HIGH>
+static cudaError_t launch_tc_kc(const AttnParams& p, int vec16, cudaStream_t s) {
+  switch (chunk_slots(p.topk)) {
+    case 1: return launch_tc_t<DP, 1, TIE_HIGH>(p, vec16, s);
+    case 2: return launch_tc_t<DP, 2, TIE_HIGH>(p, vec16, s);
+    case 4: return launch_tc_t<DP, 4, TIE_HIGH>(p, vec16, s);
+    default: return launch_tc_t<DP, 8, TIE_HIGH>(p, vec16, s);
+  }
+}
+
+// bf16, N >= 128, k <= 8: is the tensor-core top-k path available?
+bool topk_tc_supported(const AttnParams& p) {
+  return p.N >= 128 && p.d <= 128 && p.topk <= 8;
+}
+
+cudaError_t launch_topk_tc(const AttnParams& p, bool tie_high, cudaStream_t s) {
+  // 16-byte staging copies need d % 8 == 0 and 16-byte aligned rows
+  const uintptr_t qa = reinterpret_cast<uintptr_t>(p.q);
+  const uintptr_t ka = reinterpret_cast<uintptr_t>(p.k);
+  const int vec16 = (p.d % 8 == 0) && (qa % 16 == 0) && (ka % 16 == 0) &&
+                    (p.st.qn % 8 == 0) && (p.st.kn % 8 == 0) &&
+                    (p.st.qb % 8 == 0) && (p.st.kb % 8 == 0);
+  const int dp = p.d <= 16 ? 16 : p.d <= 32 ? 32 : p.d <= 64 ? 64 : 128;
+  switch (dp) {
+    case 16: return tie_high ? launch_tc_kc<16, true>(p, vec16, s) : launch_tc_kc<16, false>(p, vec16, s);
+    case 32: return tie_high ? launch_tc_kc<32, true>(p, vec16, s) : launch_tc_kc<32, false>(p, vec16, s);
+    case 64: return tie_high ? launch_tc_kc<64, true>(p, vec16, s) : launch_tc_kc<64, false>(p, vec16, s);
+    default: return tie_high ? launch_tc_kc<128, true>(p, vec16, s) : launch_tc_kc<128, false>(p, vec16, s);
+  }
+}
+
+}  // namespace tarmac
