@@ -16,14 +16,17 @@
 //   current one is scored.
 // * Per 128-key round one thread issues tcgen05.mma (M = 128, N <= 128,
 //   K = 16 per instruction) for the 128 x 128 score tile into 128 TMEM
-//   columns and commits it to an mbarrier; a block holds 128 columns, so four
-//   blocks share an SM's TMEM and overlap each other's load, MMA and scan.
-// * Every thread scans its row's scores (tcgen05.ld, 32 columns at a time)
-//   in increasing key order and keeps the exact k best in a sorted register
-//   list: later keys enter only if they beat the last entry (strictly for the
-//   lowest-index rule, or on ties for the highest-index rule). A warp vote per
-//   key skips the insertion wherever no lane needs it. Masked keys (the
-//   diagonal, the padding beyond N) read as NaN, which beats nothing.
+//   columns and commits it to an mbarrier; a block holds 128 columns, so up
+//   to four blocks share an SM's TMEM and overlap each other's phases.
+// * Pass 1 (per round): every thread reads its row's scores (tcgen05.ld, 32
+//   columns at a time), forms the maximum of each chunk of CH keys and keeps
+//   the KC >= k best chunks (the k best scores lie in them). A chunk that
+//   enters the list has its CH scores saved to the row's shared-memory slot
+//   of the chunk it evicts. Masked keys (the diagonal, the padding beyond N)
+//   read as NaN, which no comparison accepts.
+// * Pass 2 (after the last round): every thread rescans only its KC saved
+//   chunks, in increasing key order, and keeps the exact k best under the
+//   tie rule.
 // * Softmax over the k retained scores, weighted sum of their V rows
 //   gathered from global memory, store.
 #include "tc_common.cuh"
@@ -35,15 +38,49 @@ constexpr int TC_THREADS = 128;
 constexpr int TC_TILE = 128;          // keys per round
 constexpr int TC_MIN_SMEM = 50 << 10; // caps residency at 4 blocks per SM
 
+// keys per chunk for a list of KC chunks: the saved scores take 64 floats
+// per row (32 for KC = 1)
+__host__ __device__ constexpr int tc_chunk(int KC) {
+  return KC <= 2 ? 32 : (KC == 4 ? 16 : 8);
+}
+
+// Insert chunk (cm, cid) into the descending list (mv, mc, ms) of KC chunks
+// under the streaming tie rule; the dropped last entry's slot goes to the
+// new chunk.
+template <int KC, bool TIE_HIGH>
+__device__ __forceinline__ void chunk_insert(float (&mv)[KC], int (&mc)[KC],
+                                             int (&ms)[KC], float cm, int cid,
+                                             int slot) {
+#pragma unroll
+  for (int p = KC - 1; p >= 1; --p) {
+    const bool here = beats<TIE_HIGH>(cm, mv[p]);
+    const bool above = beats<TIE_HIGH>(cm, mv[p - 1]);
+    mv[p] = above ? mv[p - 1] : (here ? cm : mv[p]);
+    mc[p] = above ? mc[p - 1] : (here ? cid : mc[p]);
+    ms[p] = above ? ms[p - 1] : (here ? slot : ms[p]);
+  }
+  if (beats<TIE_HIGH>(cm, mv[0])) {
+    mv[0] = cm;
+    mc[0] = cid;
+    ms[0] = slot;
+  }
+}
+
 template <int DP, int KC, bool TIE_HIGH>
 __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     topk_tc_kernel(AttnParams p, int vec16) {
   using T = __nv_bfloat16;
-  constexpr int KCH = DP / 8;  // 16-byte chunks per row
+  constexpr int KCH = DP / 8;  // 16-byte chunks per bf16 row
   constexpr int TILE_BYTES = TC_TILE * DP * 2;
-  extern __shared__ __align__(1024) unsigned char tc_smem[];
+  constexpr int CH = tc_chunk(KC);
+  constexpr int G = CH / 4;    // float4 groups per chunk
+  constexpr int RG = KC * G;   // float4 groups per row's slots
+  extern __shared__ __align__(16) unsigned char tc_smem[];
   unsigned char* sQ = tc_smem;                  // 128 x DP bf16
   unsigned char* sK = sQ + TILE_BYTES;          // 2 slots of 128 x DP bf16
+  // saved chunks: row r's KC slots at sv + r * (RG + 1); the one-float4 pad
+  // puts the 8 lanes of a 128-byte wavefront on 8 distinct bank groups
+  float4* sv = reinterpret_cast<float4*>(sK + 2 * TILE_BYTES);
   __shared__ __align__(8) uint64_t mbar;
   __shared__ uint32_t tmem_sh;
 
@@ -69,14 +106,16 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     tc::mbar_init_fence();
   }
 
-  // padding rows (i >= N) start full of +inf entries and so insert nothing
-  float bs[KC];
-  int bi[KC];
+  // chunk list; padding rows (i >= N) start full of +inf and admit nothing
+  float mv[KC];
+  int mc[KC], ms[KC];
 #pragma unroll
   for (int m = 0; m < KC; ++m) {
-    bs[m] = i < N ? -INFINITY : INFINITY;
-    bi[m] = -1;
+    mv[m] = i < N ? -INFINITY : INFINITY;
+    mc[m] = -1;
+    ms[m] = m;
   }
+  float4* my_slots = sv + row * (RG + 1);
 
   const int rounds = cdiv(N, TC_TILE);
   const uint32_t qa = tc::smem_addr(sQ), ka = tc::smem_addr(sK);
@@ -117,17 +156,31 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
       float v[32];
       tc::tmem_ld32(tmem + lane_off + c * 32, v);
       const int j0 = k0 + c * 32;
-      // warp-uniform: this chunk holds the warp's diagonal or the padding
+      // warp-uniform: these columns hold the warp's diagonal or the padding
       if (j0 + 32 > N || j0 == q0 + warp * 32) {
 #pragma unroll
         for (int t = 0; t < 32; ++t)
           if (j0 + t >= N || j0 + t == i) v[t] = qnan;
       }
 #pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        const bool hit = beats<TIE_HIGH>(v[t], bs[KC - 1]);
-        if (__any_sync(0xffffffffu, hit)) {
-          if (hit) buf_insert<KC, TIE_HIGH>(bs, bi, v[t], j0 + t);
+      for (int u = 0; u < 32 / CH; ++u) {
+        float cm = v[u * CH];
+#pragma unroll
+        for (int t = 1; t + 1 < CH; t += 2)
+          cm = max3f(cm, v[u * CH + t], v[u * CH + t + 1]);
+        cm = fmaxf(cm, v[u * CH + CH - 1]);
+        const bool enter = beats<TIE_HIGH>(cm, mv[KC - 1]);
+        if (__any_sync(0xffffffffu, enter)) {
+          if (enter) {
+            const int slot = ms[KC - 1];
+            float4* dst = my_slots + slot * G;
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+              dst[g] = make_float4(v[u * CH + 4 * g], v[u * CH + 4 * g + 1],
+                                   v[u * CH + 4 * g + 2], v[u * CH + 4 * g + 3]);
+            chunk_insert<KC, TIE_HIGH>(mv, mc, ms, cm, (j0 + u * CH) / CH,
+                                       slot);
+          }
         }
       }
     }
@@ -136,6 +189,44 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
   __syncthreads();
   if (warp == 0) tc::tmem_dealloc(tmem, TC_TILE);
   if (i >= N) return;
+
+  // ---- pass 2: exact k best among the saved chunks ------------------------
+  // The saved chunks, visited in increasing key order, are a stream holding
+  // the k best scores of the row; the streaming insert keeps them under the
+  // tie rule. Empty entries (mc < 0) sort last and are skipped.
+#pragma unroll
+  for (int a = 0; a < KC; ++a)
+#pragma unroll
+    for (int m = 0; m + 1 < KC - a; ++m) {
+      const unsigned x = (unsigned)mc[m], y = (unsigned)mc[m + 1];
+      const bool sw = x > y;
+      mc[m] = sw ? (int)y : (int)x;
+      mc[m + 1] = sw ? (int)x : (int)y;
+      const int t = ms[m];
+      ms[m] = sw ? ms[m + 1] : t;
+      ms[m + 1] = sw ? t : ms[m + 1];
+    }
+  float bs[KC];
+  int bi[KC];
+#pragma unroll
+  for (int m = 0; m < KC; ++m) {
+    bs[m] = -INFINITY;
+    bi[m] = -1;
+  }
+#pragma unroll
+  for (int m = 0; m < KC; ++m) {
+    if (mc[m] < 0) break;
+    const int jb = mc[m] * CH;
+    const float4* src = my_slots + ms[m] * G;
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      const float4 f = src[g];
+      buf_insert<KC, TIE_HIGH>(bs, bi, f.x, jb + 4 * g);
+      buf_insert<KC, TIE_HIGH>(bs, bi, f.y, jb + 4 * g + 1);
+      buf_insert<KC, TIE_HIGH>(bs, bi, f.z, jb + 4 * g + 2);
+      buf_insert<KC, TIE_HIGH>(bs, bi, f.w, jb + 4 * g + 3);
+    }
+  }
 
   // ---- softmax over the k retained scores, V gather-aggregate -------------
   const int kk = p.topk;
@@ -193,7 +284,8 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
 
 template <int DP, int KC, bool TIE_HIGH>
 static cudaError_t launch_tc_t(const AttnParams& p, int vec16, cudaStream_t s) {
-  const size_t need = (size_t)3 * TC_TILE * DP * 2;
+  const size_t need = (size_t)3 * TC_TILE * DP * 2 +
+                      (size_t)128 * (KC * tc_chunk(KC) + 4) * 4;
   const size_t sm = need > (size_t)TC_MIN_SMEM ? need : (size_t)TC_MIN_SMEM;
   cudaError_t e = cudaFuncSetAttribute(topk_tc_kernel<DP, KC, TIE_HIGH>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
