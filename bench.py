@@ -63,8 +63,9 @@ def _peaks() -> dict:
     f = REPO / "MEASURED_PEAKS.json"
     if f.exists():
         d = json.loads(f.read_text())
-        return {"hbm_gbs": d["hbm_gbs"], "src": "measured"}
-    return {"hbm_gbs": 6650.0, "src": "fallback"}
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
 # ---------------------------------------------------------------------------
@@ -248,6 +249,41 @@ def _time_loop(fn, steps: int, stream) -> float:
     return e0.elapsed_time(e1)
 
 
+def _sweep_c5(ops, dev, stream) -> list:
+    """bf16 batch-scaling grid at B=4096 episodes on this GPU: dense and
+    top-k (k = 1, 2) through the tensor-core kernels. Informational rows
+    (inputs > L2 at N=512; 10 reps after one warm-up call)."""
+    import torch
+    peaks = _peaks()
+    rows = []
+    B = 4096
+    for n_ in (128, 512):
+        for d_ in (16, 32, 64):
+            gs = torch.Generator().manual_seed(1234 + 7 * n_ + d_)
+            q_, k_, v_ = (torch.randn(B, n_, d_, generator=gs).to(torch.bfloat16).to(dev)
+                          for _ in range(3))
+            row = {"B": B, "N": n_, "d": d_}
+            reps = 10
+            ops.dense_attention(q_, k_, v_)
+            t = _time_loop(lambda s: ops.dense_attention(q_, k_, v_), reps, stream) / reps
+            flops = 4.0 * B * n_ * n_ * d_
+            byts = 4.0 * B * n_ * d_ * 2
+            row["dense_us"] = round(1e3 * t, 2)
+            row["dense_tflops"] = round(flops / (t * 1e-3) / 1e12, 1)
+            row["dense_frac_bf16_peak"] = round(flops / (t * 1e-3) / 1e12
+                                                / peaks["bf16_tflops"], 3)
+            row["dense_hbm_frac"] = round(byts / (t * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)
+            for kk_ in (1, 2):
+                ops.topk_attention(q_, k_, v_, kk_)
+                t = _time_loop(lambda s: ops.topk_attention(q_, k_, v_, kk_), reps,
+                               stream) / reps
+                row[f"topk_k{kk_}_us"] = round(1e3 * t, 2)
+            row["agent_rows_per_s_topk_k2"] = B * n_ / (row["topk_k2_us"] * 1e-6)
+            rows.append(row)
+            del q_, k_, v_
+    return rows
+
+
 def _fp32_peak(dev) -> float:
     """Measured fp32 (TF32 off) cuBLAS GEMM TFLOP/s: the FFMA roof the fp32
     top-k kernel is bound by (not a tensor-core figure)."""
@@ -411,6 +447,8 @@ def run_ours(args) -> int:
             t = _time_loop(lambda s: ops.dense_attention(q_, k_, v_), reps, stream) / reps
             row["dense_us"] = round(1e3 * t, 2)
             sweep.append(row)
+        del q_, k_, v_
+    sweep_c5 = _sweep_c5(ops, dev, stream) if rank == 0 and not args.no_sweep else []
 
     fp32_tf = _fp32_peak(dev) if rank == 0 else None
     if multi:
@@ -457,6 +495,7 @@ def run_ours(args) -> int:
                                          "TF32 off, this run"},
         "clocks": clk.summary(),
         "sweep_c2_us": sweep,
+        "sweep_c5_bf16": sweep_c5,
     }
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(args.cpu_episodes, args.cpu_seconds)

@@ -186,7 +186,14 @@ static cudaError_t launch_dense_dt(const AttnParams& p, cudaStream_t s) {
   return launch_dense_dp<128, T>(p, s);
 }
 
+bool dense_tc_supported(const AttnParams& p);
+cudaError_t launch_dense_tc(const AttnParams& p, cudaStream_t s);
+
+// bf16 episodes of 128 or more agents run on the tensor cores (dense_tc.cu);
+// fp32 inputs and small bf16 episodes on the packed-FMA kernel above.
 cudaError_t launch_dense(const AttnParams& p, int dtype, cudaStream_t s) {
+  if (dtype == TARMAC_BF16 && dense_tc_supported(p))
+    return launch_dense_tc(p, s);
   return dtype == TARMAC_BF16 ? launch_dense_dt<__nv_bfloat16>(p, s)
                               : launch_dense_dt<float>(p, s);
 }

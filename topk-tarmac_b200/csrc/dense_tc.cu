@@ -1,0 +1,272 @@
+// dense_tc.cu — dense masked-diagonal attention for bf16 inputs on the
+// fifth-generation tensor cores (tcgen05, TMEM accumulators).
+//
+// Same function as dense.cu and the reference's _flash_dense_kernel
+// (src/kernels/fused_dense_attention.py:38-99): softmax(q k^T * scale) v with
+// the diagonal excluded, an online softmax, no score matrix in global memory.
+// bf16 x bf16 products accumulate in fp32 (the reference's bf16 path); the
+// softmax weights enter the second product as bf16, as the reference's
+// `tl.dot(p.to(v.dtype), v)` does.
+//
+// One block (4 warps) owns 128 queries of one episode; thread t of warp w
+// owns query row 32*w + t, its TMEM lane. Per tile of 64 keys:
+// * S = Q K^T (M = 128, N = 64) into TMEM columns [0, 64), issued by one
+//   thread as soon as the tile's K is staged.
+// * Each thread reads its 64 scores, masks the diagonal and the padding,
+//   and updates a base-2 online softmax whose reference maximum moves only
+//   when a score exceeds it by more than 2^8 (the stale maximum bounds every
+//   weight by 2^8; the final division cancels the reference point). When it
+//   moves, the thread rescales its row of the output accumulator in TMEM.
+//   The weights go to shared memory as bf16 in the K-major A-operand layout.
+// * O += P V (M = 128, N = d, K = 64) into TMEM columns [64, 64 + d), with
+//   V staged MN-major (its rows are the contraction dimension).
+// K and V tiles stream through a two-slot ring with 16-byte cp.async; the
+// next tile loads while the current one is in the softmax. The tile's
+// product P V and the next tile's Q K^T are issued together.
+#include "tc_common.cuh"
+
+namespace tarmac {
+
+constexpr int DTC_THREADS = 128;
+constexpr int DTC_KEYS = 64;  // keys per tile
+constexpr float DTC_LOG2E = 1.4426950408889634f;
+constexpr float DTC_RESCALE_LOG2 = 8.0f;
+
+template <int DP>
+__host__ __device__ constexpr int dtc_tmem_cols() {
+  return DTC_KEYS + DP <= 128 ? 128 : 256;
+}
+
+template <int DP>
+__host__ __device__ constexpr size_t dtc_smem_bytes() {
+  return (size_t)128 * DP * 2            // Q
+         + (size_t)2 * DTC_KEYS * DP * 2 // K ring
+         + (size_t)2 * DTC_KEYS * DP * 2 // V ring
+         + (size_t)128 * DTC_KEYS * 2;   // P
+}
+
+template <int DP>
+__global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
+    dense_tc_kernel(AttnParams p, int vec16) {
+  using T = __nv_bfloat16;
+  constexpr int KCH = DP / 8;               // 16-byte chunks per Q/K row
+  constexpr int QB = 128 * DP * 2;          // bytes of Q
+  constexpr int KB = DTC_KEYS * DP * 2;     // bytes of one K or V tile
+  constexpr int PCH = DTC_KEYS / 8;         // 16-byte chunks per P row
+  extern __shared__ __align__(16) unsigned char dtc_smem[];
+  unsigned char* sQ = dtc_smem;
+  unsigned char* sK = sQ + QB;              // 2 slots
+  unsigned char* sV = sK + 2 * KB;          // 2 slots
+  unsigned char* sP = sV + 2 * KB;          // 128 x 64 bf16, K-major
+  __shared__ __align__(8) uint64_t mbar_s, mbar_pv;
+  __shared__ uint32_t tmem_sh;
+
+  const int N = p.N, d = p.d;
+  const int qblocks = cdiv(N, 128);
+  const int b = blockIdx.x / qblocks;
+  const int q0 = (blockIdx.x - b * qblocks) * 128;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row = warp * 32 + lane;
+  const int i = q0 + row;
+  const bool vec = p.vec != 0;
+  const bool v16 = vec16 != 0;
+
+  const T* Q = static_cast<const T*>(p.q) + (int64_t)b * p.st.qb;
+  const T* K = static_cast<const T*>(p.k) + (int64_t)b * p.st.kb;
+  const T* V = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
+  T* O = static_cast<T*>(p.o) + (int64_t)b * p.st.ob;
+
+  tc::stage_kmajor<DP>(sQ, Q, p.st.qn, q0, 128, N, d, v16);
+  tc::stage_kmajor<DP>(sK, K, p.st.kn, 0, DTC_KEYS, N, d, v16);
+  tc::stage_mnmajor<DP>(sV, V, p.st.vn, 0, DTC_KEYS, N, d, v16);
+  if (warp == 0) tc::tmem_alloc(&tmem_sh, dtc_tmem_cols<DP>());
+  if (threadIdx.x == 0) {
+    tc::mbar_init(&mbar_s, 1);
+    tc::mbar_init(&mbar_pv, 1);
+    tc::mbar_init_fence();
+  }
+  cp_async_wait_all();
+  tc::fence_async_smem();
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = tmem_sh;
+  const uint32_t t_s = tmem, t_o = tmem + DTC_KEYS;
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t qa = tc::smem_addr(sQ), ka = tc::smem_addr(sK),
+                 va = tc::smem_addr(sV), pa = tc::smem_addr(sP);
+  const uint32_t idesc_s = tc::idesc_bf16(128, DTC_KEYS, false, false);
+  const uint32_t idesc_o = tc::idesc_bf16(128, DP, false, true);
+
+  auto issue_s = [&](int slot) {
+#pragma unroll
+    for (int ks = 0; ks < DP / 16; ++ks)
+      tc::mma_bf16(t_s, tc::smem_desc(qa + ks * 256, 128, KCH * 128),
+                   tc::smem_desc(ka + slot * KB + ks * 256, 128, KCH * 128),
+                   idesc_s, ks > 0);
+    tc::mma_commit(&mbar_s);
+  };
+  if (threadIdx.x == 0) issue_s(0);
+
+  const float c2 = p.qscale * p.post_scale * DTC_LOG2E;
+  float mref = -1e30f;         // reference maximum in exponent units
+  float mth = -INFINITY;       // raw score above which the reference moves
+  float l = 0.f;
+  bool ok = true;
+  const int tiles = cdiv(N, DTC_KEYS);
+  int pv_waited = -1;          // last P V product known complete
+  unsigned char* prow = sP + (row >> 3) * PCH * 128 + (row & 7) * 16;
+
+  for (int j = 0; j < tiles; ++j) {
+    const int k0 = j * DTC_KEYS;
+    if (j + 1 < tiles) {
+      // slot (j + 1) & 1 was last read by tile j - 1's products
+      if (j >= 1 && pv_waited < j - 1) {
+        ok &= tc::mbar_wait(&mbar_pv, (uint32_t)((j - 1) & 1));
+        pv_waited = j - 1;
+      }
+      const int sl = (j + 1) & 1;
+      tc::stage_kmajor<DP>(sK + sl * KB, K, p.st.kn, k0 + DTC_KEYS, DTC_KEYS,
+                           N, d, v16);
+      tc::stage_mnmajor<DP>(sV + sl * KB, V, p.st.vn, k0 + DTC_KEYS,
+                            DTC_KEYS, N, d, v16);
+    }
+    ok &= tc::mbar_wait(&mbar_s, (uint32_t)(j & 1));
+    tc::fence_after_sync();
+    float s[DTC_KEYS];
+    {
+      float h[32];
+      tc::tmem_ld32(t_s + lane_off, h);
+#pragma unroll
+      for (int t = 0; t < 32; ++t) s[t] = h[t];
+      tc::tmem_ld32(t_s + lane_off + 32, h);
+#pragma unroll
+      for (int t = 0; t < 32; ++t) s[32 + t] = h[t];
+    }
+    // warp-uniform: the tile holds padding or this warp's diagonal
+    if (k0 + DTC_KEYS > N || (k0 < q0 + warp * 32 + 32 && q0 + warp * 32 < k0 + DTC_KEYS)) {
+#pragma unroll
+      for (int t = 0; t < DTC_KEYS; ++t)
+        if (k0 + t >= N || k0 + t == i) s[t] = -INFINITY;
+    }
+    float mt = s[0];
+#pragma unroll
+    for (int t = 1; t + 1 < DTC_KEYS; t += 2) mt = max3f(mt, s[t], s[t + 1]);
+    mt = fmaxf(mt, s[DTC_KEYS - 1]);
+
+    // P and the accumulator are free once tile j - 1's P V has completed
+    if (j >= 1 && pv_waited < j - 1) {
+      ok &= tc::mbar_wait(&mbar_pv, (uint32_t)((j - 1) & 1));
+      pv_waited = j - 1;
+    }
+    tc::fence_after_sync();
+    const bool move = mt > mth;
+    float alpha = 1.0f;
+    if (move) {
+      const float mn = mt * c2;
+      alpha = exp2f(mref - mn);
+      l *= alpha;
+      mref = mn;
+      mth = mt + DTC_RESCALE_LOG2 / c2;
+    }
+    // TMEM loads and stores are warp-collective: the whole warp rescales
+    // when any lane moved its reference (the others multiply by 1)
+    if (j > 0 && __any_sync(0xffffffffu, move)) {
+#pragma unroll
+      for (int c = 0; c < DP; c += 8) {
+        float o8[8];
+        tc::tmem_ld8(t_o + lane_off + c, o8);
+#pragma unroll
+        for (int u = 0; u < 8; ++u) o8[u] *= alpha;
+        tc::tmem_st8(t_o + lane_off + c, o8);
+      }
+    }
+#pragma unroll
+    for (int c = 0; c < PCH; ++c) {
+      float e[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        e[u] = exp2f(fmaf(s[8 * c + u], c2, -mref));
+        l += e[u];
+      }
+      uint4 w;
+      w.x = tc::pack_bf16x2(e[0], e[1]);
+      w.y = tc::pack_bf16x2(e[2], e[3]);
+      w.z = tc::pack_bf16x2(e[4], e[5]);
+      w.w = tc::pack_bf16x2(e[6], e[7]);
+      *reinterpret_cast<uint4*>(prow + c * 128) = w;
+    }
+    // K and V of tile j + 1 have landed (this thread's copies); P is written
+    cp_async_wait_all();
+    tc::fence_async_smem();
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    if (threadIdx.x == 0) {
+      const int sl = j & 1;
+#pragma unroll
+      for (int ks = 0; ks < DTC_KEYS / 16; ++ks)
+        tc::mma_bf16(t_o, tc::smem_desc(pa + ks * 256, 128, PCH * 128),
+                     tc::smem_desc(va + sl * KB + ks * 256, 128,
+                                   DTC_KEYS * 16),
+                     idesc_o, j > 0 || ks > 0);
+      tc::mma_commit(&mbar_pv);
+      if (j + 1 < tiles) issue_s((j + 1) & 1);
+    }
+  }
+  if (pv_waited < tiles - 1)
+    ok &= tc::mbar_wait(&mbar_pv, (uint32_t)((tiles - 1) & 1));
+  tc::fence_after_sync();
+
+  float o[DP];
+#pragma unroll
+  for (int c = 0; c < DP; c += 8) {
+    float o8[8];
+    tc::tmem_ld8(t_o + lane_off + c, o8);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) o[c + u] = o8[u];
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 0) tc::tmem_dealloc(tmem, dtc_tmem_cols<DP>());
+  if (i >= N) return;
+  const float inv = 1.0f / l;
+#pragma unroll
+  for (int c = 0; c < DP; ++c)
+    o[c] = ok ? o[c] * inv : __int_as_float(0x7fc00000);
+  store_row<DP, T>(O + (int64_t)i * p.st.on, o, d, vec);
+}
+
+template <int DP>
+static cudaError_t launch_dtc(const AttnParams& p, int vec16, cudaStream_t s) {
+  const size_t sm = dtc_smem_bytes<DP>();
+  cudaError_t e = cudaFuncSetAttribute(
+      dense_tc_kernel<DP>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = (int64_t)p.B * cdiv(p.N, 128);
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  dense_tc_kernel<DP><<<(unsigned)blocks, DTC_THREADS, sm, s>>>(p, vec16);
+  return cudaGetLastError();
+}
+
+// bf16, N >= 128: is the tensor-core dense path available?
+bool dense_tc_supported(const AttnParams& p) {
+  return p.N >= 128 && p.d <= 128;
+}
+
+cudaError_t launch_dense_tc(const AttnParams& p, cudaStream_t s) {
+  const uintptr_t qa = reinterpret_cast<uintptr_t>(p.q);
+  const uintptr_t ka = reinterpret_cast<uintptr_t>(p.k);
+  const uintptr_t va = reinterpret_cast<uintptr_t>(p.v);
+  const int vec16 = (p.d % 8 == 0) && (qa % 16 == 0) && (ka % 16 == 0) &&
+                    (va % 16 == 0) && (p.st.qn % 8 == 0) &&
+                    (p.st.kn % 8 == 0) && (p.st.vn % 8 == 0) &&
+                    (p.st.qb % 8 == 0) && (p.st.kb % 8 == 0) &&
+                    (p.st.vb % 8 == 0);
+  if (p.d <= 16) return launch_dtc<16>(p, vec16, s);
+  if (p.d <= 32) return launch_dtc<32>(p, vec16, s);
+  if (p.d <= 64) return launch_dtc<64>(p, vec16, s);
+  return launch_dtc<128>(p, vec16, s);
+}
+
+}  // namespace tarmac

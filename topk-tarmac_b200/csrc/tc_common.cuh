@@ -170,6 +170,12 @@ __device__ __forceinline__ void tmem_st8(uint32_t taddr, const float (&v)[8]) {
       : "memory");
 }
 
+// two fp32 values as a bf16 pair (round to nearest even), a in the low half
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
 // byte offset of row r, 16-byte chunk c in a K-major core-matrix tile with
 // KC chunks per row
 __device__ __forceinline__ uint32_t kmajor_off(int r, int c, int KC) {
@@ -191,6 +197,45 @@ __device__ __forceinline__ void stage_kmajor(unsigned char* tile,
   for (int e = threadIdx.x; e < nrows * KC; e += blockDim.x) {
     const int r = e / KC, c = e - (e / KC) * KC;
     const uint32_t off = kmajor_off(r, c, KC);
+    const int gr = r0 + r;
+    const int c0 = c * 8;
+    if (gr < rlimit && c0 < d) {
+      const __nv_bfloat16* g = src + (int64_t)gr * rs + c0;
+      if (vec) {
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(base + off),
+                     "l"(g)
+                     : "memory");
+      } else {
+        __nv_bfloat16 t[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          t[u] = (c0 + u < d) ? g[u] : __float2bfloat16_rn(0.f);
+        *reinterpret_cast<uint4*>(tile + off) = *reinterpret_cast<uint4*>(t);
+      }
+    } else {
+      *reinterpret_cast<uint4*>(tile + off) = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+
+// Stage rows [r0, r0 + nrows) of a [*, d] bf16 matrix (row stride rs) as the
+// MN-major B operand of a product that contracts over those rows: element
+// (row k, column n) goes to byte ((k / 8) + (n / 8) * (nrows / 8)) * 128 +
+// (k % 8) * 16 + (n % 8) * 2 (leading-dimension offset 128 B along k,
+// stride-dimension offset nrows * 16 B along n). Rows >= rlimit and columns
+// >= d are zero. nrows is a multiple of 8.
+template <int DP>
+__device__ __forceinline__ void stage_mnmajor(unsigned char* tile,
+                                              const __nv_bfloat16* src,
+                                              int64_t rs, int r0, int nrows,
+                                              int rlimit, int d, bool vec) {
+  constexpr int KC = DP / 8;
+  const uint32_t base = smem_addr(tile);
+  for (int e = threadIdx.x; e < nrows * KC; e += blockDim.x) {
+    const int r = e / KC, c = e - (e / KC) * KC;
+    const uint32_t off =
+        (uint32_t)(((r >> 3) + c * (nrows >> 3)) * 128 + (r & 7) * 16);
     const int gr = r0 + r;
     const int c0 = c * 8;
     if (gr < rlimit && c0 < d) {
