@@ -22,7 +22,9 @@
 //   V staged MN-major (its rows are the contraction dimension).
 // K and V tiles stream through a two-slot ring with 16-byte cp.async; the
 // next tile loads while the current one is in the softmax. The tile's
-// product P V and the next tile's Q K^T are issued together.
+// product P V and the next tile's Q K^T are issued together. The weights
+// come from ex2.approx (relative error ~2^-22, far below their bf16
+// rounding).
 #include "tc_common.cuh"
 
 namespace tarmac {
@@ -76,9 +78,26 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
   const T* V = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
   T* O = static_cast<T*>(p.o) + (int64_t)b * p.st.ob;
 
-  tc::stage_kmajor<DP>(sQ, Q, p.st.qn, q0, 128, N, d, v16);
-  tc::stage_kmajor<DP>(sK, K, p.st.kn, 0, DTC_KEYS, N, d, v16);
-  tc::stage_mnmajor<DP>(sV, V, p.st.vn, 0, DTC_KEYS, N, d, v16);
+  const uint32_t qa = tc::smem_addr(sQ), ka = tc::smem_addr(sK),
+                 va = tc::smem_addr(sV), pa = tc::smem_addr(sP);
+  // K and V rows [r0, r0 + 64) into ring slot sl
+  auto stage_kv = [&](int sl, int r0) {
+    if (v16) {
+      tc::stage_fast<DP, DTC_KEYS, false>(ka + sl * KB, K + (int64_t)r0 * p.st.kn,
+                                          p.st.kn, N - r0, d);
+      tc::stage_fast<DP, DTC_KEYS, true>(va + sl * KB, V + (int64_t)r0 * p.st.vn,
+                                         p.st.vn, N - r0, d);
+    } else {
+      tc::stage_kmajor<DP>(sK + sl * KB, K, p.st.kn, r0, DTC_KEYS, N, d, false);
+      tc::stage_mnmajor<DP>(sV + sl * KB, V, p.st.vn, r0, DTC_KEYS, N, d, false);
+    }
+  };
+  if (v16)
+    tc::stage_fast<DP, 128, false>(qa, Q + (int64_t)q0 * p.st.qn, p.st.qn,
+                                   N - q0, d);
+  else
+    tc::stage_kmajor<DP>(sQ, Q, p.st.qn, q0, 128, N, d, false);
+  stage_kv(0, 0);
   if (warp == 0) tc::tmem_alloc(&tmem_sh, dtc_tmem_cols<DP>());
   if (threadIdx.x == 0) {
     tc::mbar_init(&mbar_s, 1);
@@ -93,8 +112,6 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
   const uint32_t tmem = tmem_sh;
   const uint32_t t_s = tmem, t_o = tmem + DTC_KEYS;
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-  const uint32_t qa = tc::smem_addr(sQ), ka = tc::smem_addr(sK),
-                 va = tc::smem_addr(sV), pa = tc::smem_addr(sP);
   const uint32_t idesc_s = tc::idesc_bf16(128, DTC_KEYS, false, false);
   const uint32_t idesc_o = tc::idesc_bf16(128, DP, false, true);
 
@@ -125,11 +142,7 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
         ok &= tc::mbar_wait(&mbar_pv, (uint32_t)((j - 1) & 1));
         pv_waited = j - 1;
       }
-      const int sl = (j + 1) & 1;
-      tc::stage_kmajor<DP>(sK + sl * KB, K, p.st.kn, k0 + DTC_KEYS, DTC_KEYS,
-                           N, d, v16);
-      tc::stage_mnmajor<DP>(sV + sl * KB, V, p.st.vn, k0 + DTC_KEYS,
-                            DTC_KEYS, N, d, v16);
+      stage_kv((j + 1) & 1, k0 + DTC_KEYS);
     }
     ok &= tc::mbar_wait(&mbar_s, (uint32_t)(j & 1));
     tc::fence_after_sync();
@@ -164,7 +177,7 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
     float alpha = 1.0f;
     if (move) {
       const float mn = mt * c2;
-      alpha = exp2f(mref - mn);
+      alpha = tc::ex2_approx(mref - mn);
       l *= alpha;
       mref = mn;
       mth = mt + DTC_RESCALE_LOG2 / c2;
@@ -186,7 +199,7 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
       float e[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        e[u] = exp2f(fmaf(s[8 * c + u], c2, -mref));
+        e[u] = tc::ex2_approx(fmaf(s[8 * c + u], c2, -mref));
         l += e[u];
       }
       uint4 w;

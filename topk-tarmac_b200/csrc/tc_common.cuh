@@ -257,5 +257,144 @@ __device__ __forceinline__ void stage_mnmajor(unsigned char* tile,
   }
 }
 
+
+// Stage a full-width tile of R rows (rows r0_tile .. r0_tile + R - 1, of
+// which the first `nvalid` exist) of a [*, d] bf16 matrix with 16-byte
+// cp.async, for 128 threads, d % 8 == 0 and 16-byte aligned rows. Items are
+// taken in the K-major core-matrix order (item e = 16-byte chunk at byte
+// e * 16 of the K-major tile), so the 8 lanes of every shared-memory
+// wavefront write 128 contiguous bytes and each warp reads whole 32-byte
+// sectors of 8 or 16 rows. MN selects the MN-major destination layout of
+// stage_mnmajor (same items, other placement). Missing rows and columns
+// beyond d are written as zeros.
+template <int DP, int R, bool MN>
+__device__ __forceinline__ void stage_fast(uint32_t base,
+                                           const __nv_bfloat16* src,
+                                           int64_t rs, int nvalid, int d) {
+  constexpr int KC = DP / 8;        // chunks per row
+  constexpr int S = 128 / KC;       // rows between a thread's items
+  constexpr int U = R * KC / 128;   // items per thread
+  static_assert(U >= 1 && S % 8 == 0, "tile shape");
+  const int tid = threadIdx.x;
+  const int c = (tid >> 3) % KC;
+  const int r0 = ((tid >> 3) / KC) * 8 + (tid & 7);
+  const uint32_t off0 =
+      MN ? (uint32_t)(((r0 >> 3) + c * (R / 8)) * 128 + (r0 & 7) * 16)
+         : (uint32_t)(tid * 16);
+  constexpr uint32_t dOff = MN ? (uint32_t)(S / 8) * 128 : 2048u;
+  const bool col_ok = c * 8 < d;
+  const __nv_bfloat16* g = src + (int64_t)r0 * rs + c * 8;
+  const int64_t gstep = (int64_t)S * rs;
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const uint32_t dst = base + off0 + u * dOff;
+    if (col_ok && r0 + u * S < nvalid) {
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst),
+                   "l"(g + u * gstep)
+                   : "memory");
+    } else {
+      asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst),
+                   "r"(0u)
+                   : "memory");
+    }
+  }
+}
+
+// 2^x on the special-function unit (ex2.approx.ftz.f32: relative error
+// about 2^-22, subnormal results flushed to zero).
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+
+// Row-cooperative gather-aggregate-store over the 32 query rows of a warp.
+// Lane t owns row row0 + t: its KC candidate indices idx (used for m < kk),
+// their normalised weights w and a NaN-row flag. DP/8 lanes share a row and
+// each moves 16 bytes (8 bf16) of every gathered V row and of the output
+// row, so one warp instruction touches 32/(DP/8) whole rows rather than 32
+// scattered pieces. The owners first prefetch their V rows into L2; the
+// loads then go out in batches of up to 16 per lane before any is used.
+// Requires d % 8 == 0 and 16-byte aligned V and O rows. Every lane of the
+// warp must call it (the row data moves by shuffles).
+template <int DP, int KC>
+__device__ __forceinline__ void coop_gather_store(
+    const __nv_bfloat16* V, int64_t vn, __nv_bfloat16* O, int64_t on,
+    int row0, int N, int d, int kk, const int (&idx)[KC],
+    const float (&w)[KC], bool nan_row) {
+  constexpr int LPR = DP / 8;  // lanes per row
+  constexpr int RPI = 32 / LPR;
+  constexpr int GI = KC >= 16 ? 1 : (16 / KC < LPR ? 16 / KC : LPR);
+  const int lane = threadIdx.x & 31;
+  const int sub = lane % LPR, rsub = lane / LPR;
+  const int c0 = sub * 8;
+  if (row0 + lane < N) {
+#pragma unroll
+    for (int m = 0; m < KC; ++m)
+      if (m < kk && idx[m] >= 0) {
+        const __nv_bfloat16* vr = V + (int64_t)idx[m] * vn;
+#pragma unroll
+        for (int c = 0; c < DP; c += 64)
+          if (c < d) asm volatile("prefetch.global.L2 [%0];" ::"l"(vr + c));
+      }
+  }
+#pragma unroll
+  for (int i0 = 0; i0 < LPR; i0 += GI) {
+    uint4 raw[GI][KC];
+    float wm[GI][KC];
+    bool use[GI][KC];
+#pragma unroll
+    for (int g = 0; g < GI; ++g) {
+      const int src = (i0 + g) * RPI + rsub;
+      const bool act = row0 + src < N && c0 < d;
+#pragma unroll
+      for (int m = 0; m < KC; ++m) {
+        const int j = __shfl_sync(0xffffffffu, idx[m], src);
+        wm[g][m] = __shfl_sync(0xffffffffu, w[m], src);
+        // unused slots load row 0, column 0 (always present) and discard it
+        use[g][m] = m < kk && j >= 0 && act;
+        raw[g][m] = __ldg(reinterpret_cast<const uint4*>(
+            V + (use[g][m] ? (int64_t)j * vn + c0 : 0)));
+      }
+    }
+#pragma unroll
+    for (int g = 0; g < GI; ++g) {
+      const int src = (i0 + g) * RPI + rsub;
+      const int r = row0 + src;
+      const bool bad = __shfl_sync(0xffffffffu, (int)nan_row, src) != 0;
+      float acc[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+#pragma unroll
+      for (int m = 0; m < KC; ++m) {
+        const uint32_t h[4] = {raw[g][m].x, raw[g][m].y, raw[g][m].z,
+                               raw[g][m].w};
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float2 f = __bfloat1622float2(
+              *reinterpret_cast<const __nv_bfloat162*>(&h[u]));
+          const float a0 = fmaf(wm[g][m], f.x, acc[2 * u]);
+          const float a1 = fmaf(wm[g][m], f.y, acc[2 * u + 1]);
+          acc[2 * u] = use[g][m] ? a0 : acc[2 * u];
+          acc[2 * u + 1] = use[g][m] ? a1 : acc[2 * u + 1];
+        }
+      }
+      if (r < N && c0 < d) {
+        uint4 out;
+        if (bad) {
+          out = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+        } else {
+          out.x = pack_bf16x2(acc[0], acc[1]);
+          out.y = pack_bf16x2(acc[2], acc[3]);
+          out.z = pack_bf16x2(acc[4], acc[5]);
+          out.w = pack_bf16x2(acc[6], acc[7]);
+        }
+        *reinterpret_cast<uint4*>(O + (int64_t)r * on + c0) = out;
+      }
+    }
+  }
+}
+
 }  // namespace tc
 }  // namespace tarmac

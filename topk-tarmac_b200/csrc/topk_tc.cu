@@ -11,13 +11,14 @@
 // One block (4 warps) owns 128 queries of one episode; thread t of warp w
 // owns query row 32*w + t, which is also its tensor-memory (TMEM) lane.
 // * Q (128 x d) is staged once in shared memory as bf16 in the K-major
-//   core-matrix layout (tc_common.cuh); K streams through a two-slot ring of
-//   128-key tiles with 16-byte cp.async, the next tile loading while the
-//   current one is scored.
-// * Per 128-key round one thread issues tcgen05.mma (M = 128, N <= 128,
-//   K = 16 per instruction) for the 128 x 128 score tile into 128 TMEM
-//   columns and commits it to an mbarrier; a block holds 128 columns, so up
-//   to four blocks share an SM's TMEM and overlap each other's phases.
+//   core-matrix layout (tc_common.cuh); K streams through a ring of key
+//   tiles with 16-byte cp.async, ahead of the scan.
+// * Per round one thread issues tcgen05.mma (M = 128, K = 16 per
+//   instruction) for the round's score tile into TMEM and commits it to an
+//   mbarrier: 128-key rounds in one buffer for d <= 16; for larger d,
+//   64-key rounds in two buffers, round r + 1's product issued before round
+//   r is scanned so the tensor core works under the scan. A block holds 128
+//   TMEM columns; up to four blocks share an SM's TMEM.
 // * Pass 1 (per round): every thread reads its row's scores (tcgen05.ld, 32
 //   columns at a time), forms the maximum of each chunk of CH keys and keeps
 //   the KC >= k best chunks (the k best scores lie in them). A chunk that
@@ -27,16 +28,25 @@
 // * Pass 2 (after the last round): every thread rescans only its KC saved
 //   chunks, in increasing key order, and keeps the exact k best under the
 //   tie rule.
-// * Softmax over the k retained scores, weighted sum of their V rows
-//   gathered from global memory, store.
+// * Softmax over the k retained scores; the V gather-aggregate and the
+//   output store run row-cooperatively (DP/8 lanes per row, 16-byte
+//   coalesced pieces) when the rows allow 16-byte access.
 #include "tc_common.cuh"
 #include "topk_chunk.cuh"
 
 namespace tarmac {
 
 constexpr int TC_THREADS = 128;
-constexpr int TC_TILE = 128;          // keys per round
 constexpr int TC_MIN_SMEM = 50 << 10; // caps residency at 4 blocks per SM
+constexpr int TC_STAGE16 = 1;         // flags: 16-byte Q/K staging copies
+constexpr int TC_COOP_VO = 2;         // flags: row-cooperative V/O moves
+
+// Rounds: 128 keys in one TMEM buffer for d <= 16; 64 keys in two buffers
+// (the next round's product computing under the current scan) above that,
+// where each product is larger. The K ring holds one tile more than the
+// buffers. Both keep the block at 128 TMEM columns.
+__host__ __device__ constexpr int tc_round(int DP) { return DP <= 16 ? 128 : 64; }
+__host__ __device__ constexpr int tc_bufs(int DP) { return DP <= 16 ? 1 : 2; }
 
 // keys per chunk for a list of KC chunks: the saved scores take 64 floats
 // per row (32 for KC = 1)
@@ -68,20 +78,24 @@ __device__ __forceinline__ void chunk_insert(float (&mv)[KC], int (&mc)[KC],
 
 template <int DP, int KC, bool TIE_HIGH>
 __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
-    topk_tc_kernel(AttnParams p, int vec16) {
+    topk_tc_kernel(AttnParams p, int flags) {
   using T = __nv_bfloat16;
   constexpr int KCH = DP / 8;  // 16-byte chunks per bf16 row
-  constexpr int TILE_BYTES = TC_TILE * DP * 2;
+  constexpr int RK = tc_round(DP);
+  constexpr int NB = tc_bufs(DP);      // TMEM score buffers
+  constexpr int TC_SLOTS = NB + 1;     // K ring depth
+  constexpr int QBYTES = 128 * DP * 2;
+  constexpr int TILE_BYTES = RK * DP * 2;
   constexpr int CH = tc_chunk(KC);
   constexpr int G = CH / 4;    // float4 groups per chunk
   constexpr int RG = KC * G;   // float4 groups per row's slots
   extern __shared__ __align__(16) unsigned char tc_smem[];
   unsigned char* sQ = tc_smem;                  // 128 x DP bf16
-  unsigned char* sK = sQ + TILE_BYTES;          // 2 slots of 128 x DP bf16
+  unsigned char* sK = sQ + QBYTES;              // TC_SLOTS x RK x DP bf16
   // saved chunks: row r's KC slots at sv + r * (RG + 1); the one-float4 pad
   // puts the 8 lanes of a 128-byte wavefront on 8 distinct bank groups
-  float4* sv = reinterpret_cast<float4*>(sK + 2 * TILE_BYTES);
-  __shared__ __align__(8) uint64_t mbar;
+  float4* sv = reinterpret_cast<float4*>(sK + TC_SLOTS * TILE_BYTES);
+  __shared__ __align__(8) uint64_t mbar[2];
   __shared__ uint32_t tmem_sh;
 
   const int N = p.N, d = p.d;
@@ -91,18 +105,35 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row = warp * 32 + lane;  // TMEM lane
   const int i = q0 + row;            // query index
-  const bool vec = p.vec != 0;
+  const bool vec16 = (flags & TC_STAGE16) != 0;
 
   const T* Q = static_cast<const T*>(p.q) + (int64_t)b * p.st.qb;
   const T* K = static_cast<const T*>(p.k) + (int64_t)b * p.st.kb;
   const T* V = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
   T* O = static_cast<T*>(p.o) + (int64_t)b * p.st.ob;
 
-  tc::stage_kmajor<DP>(sQ, Q, p.st.qn, q0, 128, N, d, vec16 != 0);
-  tc::stage_kmajor<DP>(sK, K, p.st.kn, 0, TC_TILE, N, d, vec16 != 0);
-  if (warp == 0) tc::tmem_alloc(&tmem_sh, TC_TILE);
+  // K rows [r0, r0 + RK) into ring slot sl
+  auto stage_k = [&](int sl, int r0) {
+    if (vec16)
+      tc::stage_fast<DP, RK, false>(tc::smem_addr(sK) + sl * TILE_BYTES,
+                                    K + (int64_t)r0 * p.st.kn, p.st.kn, N - r0,
+                                    d);
+    else
+      tc::stage_kmajor<DP>(sK + sl * TILE_BYTES, K, p.st.kn, r0, RK, N, d,
+                           false);
+  };
+  const int rounds = cdiv(N, RK);
+  if (vec16)
+    tc::stage_fast<DP, 128, false>(tc::smem_addr(sQ), Q + (int64_t)q0 * p.st.qn,
+                                   p.st.qn, N - q0, d);
+  else
+    tc::stage_kmajor<DP>(sQ, Q, p.st.qn, q0, 128, N, d, false);
+  stage_k(0, 0);
+  if (NB == 2 && rounds > 1) stage_k(1, RK);
+  if (warp == 0) tc::tmem_alloc(&tmem_sh, NB * RK);
   if (threadIdx.x == 0) {
-    tc::mbar_init(&mbar, 1);
+    tc::mbar_init(&mbar[0], 1);
+    tc::mbar_init(&mbar[1], 1);
     tc::mbar_init_fence();
   }
 
@@ -117,44 +148,53 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
   }
   float4* my_slots = sv + row * (RG + 1);
 
-  const int rounds = cdiv(N, TC_TILE);
   const uint32_t qa = tc::smem_addr(sQ), ka = tc::smem_addr(sK);
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
   const float qnan = __int_as_float(0x7fc00000);
   bool ok = true;
   uint32_t tmem = 0;
+  // one thread: scores of round r (K in slot r % TC_SLOTS) into TMEM buffer
+  // r % NB, committed to that buffer's mbarrier
+  auto issue = [&](int r) {
+    const int nt = min(RK, cdiv(N - r * RK, 32) * 32);
+    const uint32_t kt = ka + (uint32_t)((r % TC_SLOTS) * TILE_BYTES);
+    const uint32_t idesc = tc::idesc_bf16(128, nt, false, false);
+#pragma unroll
+    for (int ks = 0; ks < DP / 16; ++ks)
+      tc::mma_bf16(tmem + (r % NB) * RK,
+                   tc::smem_desc(qa + ks * 256, 128, KCH * 128),
+                   tc::smem_desc(kt + ks * 256, 128, KCH * 128), idesc, ks > 0);
+    tc::mma_commit(&mbar[r % NB]);
+  };
+
   for (int r = 0; r < rounds; ++r) {
-    // K tile r is in its slot; every lane has finished reading round r - 1's
-    // scores from TMEM.
+    // This thread's copies of K tile r + NB - 1 (and Q at r = 0) have
+    // landed; after the barrier they are visible to the tensor core, and
+    // every lane has finished reading round r - 1's TMEM buffer.
     cp_async_wait_all();
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
-    if (r == 0) tmem = tmem_sh;
-    const int k0 = r * TC_TILE;
-    const int nt = min(TC_TILE, cdiv(N - k0, 32) * 32);  // columns this round
-    if (threadIdx.x == 0) {
-      const uint32_t kt = ka + (uint32_t)((r & 1) * TILE_BYTES);
-      const uint32_t idesc = tc::idesc_bf16(128, nt, false, false);
-#pragma unroll
-      for (int ks = 0; ks < DP / 16; ++ks) {
-        const uint64_t ad = tc::smem_desc(qa + ks * 256, 128, KCH * 128);
-        const uint64_t bd = tc::smem_desc(kt + ks * 256, 128, KCH * 128);
-        tc::mma_bf16(tmem, ad, bd, idesc, ks > 0);
-      }
-      tc::mma_commit(&mbar);
+    if (r == 0) {
+      tmem = tmem_sh;
+      if (threadIdx.x == 0) issue(0);
     }
-    // the other slot's last reader (round r - 1's MMA) has completed
-    if (r + 1 < rounds)
-      tc::stage_kmajor<DP>(sK + ((r + 1) & 1) * TILE_BYTES, K, p.st.kn,
-                           k0 + TC_TILE, TC_TILE, N, d, vec16 != 0);
-    ok &= tc::mbar_wait(&mbar, (uint32_t)(r & 1));
+    if (threadIdx.x == 0) {
+      if (NB == 2 && r + 1 < rounds) issue(r + 1);  // computes under the scan
+      if (NB == 1 && r > 0) issue(r);
+    }
+    // slot (r + NB) % TC_SLOTS last held tile r - 1, whose product completed
+    if (r + NB < rounds) stage_k((r + NB) % TC_SLOTS, (r + NB) * RK);
+    ok &= tc::mbar_wait(&mbar[r % NB], (uint32_t)((r / NB) & 1));
     tc::fence_after_sync();
 
+    const int k0 = r * RK;
+    const int nt = min(RK, cdiv(N - k0, 32) * 32);
+    const uint32_t tb = tmem + (r % NB) * RK + lane_off;
     for (int c = 0; c < nt / 32; ++c) {
       float v[32];
-      tc::tmem_ld32(tmem + lane_off + c * 32, v);
+      tc::tmem_ld32(tb + c * 32, v);
       const int j0 = k0 + c * 32;
       // warp-uniform: these columns hold the warp's diagonal or the padding
       if (j0 + 32 > N || j0 == q0 + warp * 32) {
@@ -187,8 +227,7 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 0) tc::tmem_dealloc(tmem, TC_TILE);
-  if (i >= N) return;
+  if (warp == 0) tc::tmem_dealloc(tmem, NB * RK);
 
   // ---- pass 2: exact k best among the saved chunks ------------------------
   // The saved chunks, visited in increasing key order, are a stream holding
@@ -228,7 +267,7 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     }
   }
 
-  // ---- softmax over the k retained scores, V gather-aggregate -------------
+  // ---- softmax over the k retained scores, V gather-aggregate, store ------
   const int kk = p.topk;
   const float sc = p.qscale * p.post_scale;
   const float mx = bs[0] * sc;
@@ -241,6 +280,22 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     den += e[m];
     empty |= (m < kk) && (bi[m] < 0);
   }
+  if (i < N && p.idx_out != nullptr) {
+    int32_t* io = p.idx_out + ((int64_t)b * N + i) * kk;
+#pragma unroll
+    for (int m = 0; m < KC; ++m)
+      if (m < kk) io[m] = empty ? -1 : bi[m];
+  }
+  if (flags & TC_COOP_VO) {
+    float w[KC];
+#pragma unroll
+    for (int m = 0; m < KC; ++m) w[m] = (m < kk) ? e[m] / den : 0.f;
+    tc::coop_gather_store<DP, KC>(V, p.st.vn, O, p.st.on, q0 + warp * 32, N, d,
+                                  kk, bi, w, empty);
+    return;
+  }
+  if (i >= N) return;
+  const bool vec = p.vec != 0;
   float acc[DP];
 #pragma unroll
   for (int c = 0; c < DP; ++c) acc[c] = 0.f;
@@ -274,17 +329,11 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     for (int c = 0; c < DP; ++c) acc[c] = qnan;
   }
   store_row<DP, T>(O + (int64_t)i * p.st.on, acc, d, vec);
-  if (p.idx_out != nullptr) {
-    int32_t* io = p.idx_out + ((int64_t)b * N + i) * kk;
-#pragma unroll
-    for (int m = 0; m < KC; ++m)
-      if (m < kk) io[m] = empty ? -1 : bi[m];
-  }
 }
 
 template <int DP, int KC, bool TIE_HIGH>
-static cudaError_t launch_tc_t(const AttnParams& p, int vec16, cudaStream_t s) {
-  const size_t need = (size_t)3 * TC_TILE * DP * 2 +
+static cudaError_t launch_tc_t(const AttnParams& p, int flags, cudaStream_t s) {
+  const size_t need = (size_t)(128 + (tc_bufs(DP) + 1) * tc_round(DP)) * DP * 2 +
                       (size_t)128 * (KC * tc_chunk(KC) + 4) * 4;
   const size_t sm = need > (size_t)TC_MIN_SMEM ? need : (size_t)TC_MIN_SMEM;
   cudaError_t e = cudaFuncSetAttribute(topk_tc_kernel<DP, KC, TIE_HIGH>,
@@ -294,17 +343,17 @@ static cudaError_t launch_tc_t(const AttnParams& p, int vec16, cudaStream_t s) {
   const int64_t blocks = (int64_t)p.B * cdiv(p.N, 128);
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   topk_tc_kernel<DP, KC, TIE_HIGH>
-      <<<(unsigned)blocks, TC_THREADS, sm, s>>>(p, vec16);
+      <<<(unsigned)blocks, TC_THREADS, sm, s>>>(p, flags);
   return cudaGetLastError();
 }
 
 template <int DP, bool TIE_HIGH>
-static cudaError_t launch_tc_kc(const AttnParams& p, int vec16, cudaStream_t s) {
+static cudaError_t launch_tc_kc(const AttnParams& p, int flags, cudaStream_t s) {
   switch (chunk_slots(p.topk)) {
-    case 1: return launch_tc_t<DP, 1, TIE_HIGH>(p, vec16, s);
-    case 2: return launch_tc_t<DP, 2, TIE_HIGH>(p, vec16, s);
-    case 4: return launch_tc_t<DP, 4, TIE_HIGH>(p, vec16, s);
-    default: return launch_tc_t<DP, 8, TIE_HIGH>(p, vec16, s);
+    case 1: return launch_tc_t<DP, 1, TIE_HIGH>(p, flags, s);
+    case 2: return launch_tc_t<DP, 2, TIE_HIGH>(p, flags, s);
+    case 4: return launch_tc_t<DP, 4, TIE_HIGH>(p, flags, s);
+    default: return launch_tc_t<DP, 8, TIE_HIGH>(p, flags, s);
   }
 }
 
@@ -314,18 +363,22 @@ bool topk_tc_supported(const AttnParams& p) {
 }
 
 cudaError_t launch_topk_tc(const AttnParams& p, bool tie_high, cudaStream_t s) {
-  // 16-byte staging copies need d % 8 == 0 and 16-byte aligned rows
-  const uintptr_t qa = reinterpret_cast<uintptr_t>(p.q);
-  const uintptr_t ka = reinterpret_cast<uintptr_t>(p.k);
-  const int vec16 = (p.d % 8 == 0) && (qa % 16 == 0) && (ka % 16 == 0) &&
-                    (p.st.qn % 8 == 0) && (p.st.kn % 8 == 0) &&
-                    (p.st.qb % 8 == 0) && (p.st.kb % 8 == 0);
+  const auto a16 = [](const void* x) {
+    return reinterpret_cast<uintptr_t>(x) % 16 == 0;
+  };
+  const bool d8 = p.d % 8 == 0;
+  // 16-byte staging copies of Q and K; 16-byte row moves of V and O
+  const bool qk = d8 && a16(p.q) && a16(p.k) && p.st.qn % 8 == 0 &&
+                  p.st.kn % 8 == 0 && p.st.qb % 8 == 0 && p.st.kb % 8 == 0;
+  const bool vo = d8 && a16(p.v) && a16(p.o) && p.st.vn % 8 == 0 &&
+                  p.st.on % 8 == 0 && p.st.vb % 8 == 0 && p.st.ob % 8 == 0;
+  const int flags = (qk ? TC_STAGE16 : 0) | (vo ? TC_COOP_VO : 0);
   const int dp = p.d <= 16 ? 16 : p.d <= 32 ? 32 : p.d <= 64 ? 64 : 128;
   switch (dp) {
-    case 16: return tie_high ? launch_tc_kc<16, true>(p, vec16, s) : launch_tc_kc<16, false>(p, vec16, s);
-    case 32: return tie_high ? launch_tc_kc<32, true>(p, vec16, s) : launch_tc_kc<32, false>(p, vec16, s);
-    case 64: return tie_high ? launch_tc_kc<64, true>(p, vec16, s) : launch_tc_kc<64, false>(p, vec16, s);
-    default: return tie_high ? launch_tc_kc<128, true>(p, vec16, s) : launch_tc_kc<128, false>(p, vec16, s);
+    case 16: return tie_high ? launch_tc_kc<16, true>(p, flags, s) : launch_tc_kc<16, false>(p, flags, s);
+    case 32: return tie_high ? launch_tc_kc<32, true>(p, flags, s) : launch_tc_kc<32, false>(p, flags, s);
+    case 64: return tie_high ? launch_tc_kc<64, true>(p, flags, s) : launch_tc_kc<64, false>(p, flags, s);
+    default: return tie_high ? launch_tc_kc<128, true>(p, flags, s) : launch_tc_kc<128, false>(p, flags, s);
   }
 }
 
