@@ -20,9 +20,10 @@
 //   The weights go to shared memory as bf16 in the K-major A-operand layout.
 // * O += P V (M = 128, N = d, K = 64) into TMEM columns [64, 64 + d), with
 //   V staged MN-major (its rows are the contraction dimension).
-// K and V tiles stream through a two-slot ring with 16-byte cp.async; the
-// next tile loads while the current one is in the softmax. The tile's
-// product P V and the next tile's Q K^T are issued together. The weights
+// K and V tiles stream through two-slot rings with 16-byte cp.async; the
+// next tile loads while the current one is in the softmax. The next tile's
+// Q K^T is issued ahead of the current tile's P V, so the softmax waits only
+// for its scores, and P V runs under the next softmax's exponentials. The weights
 // come from ex2.approx (relative error ~2^-22, far below their bf16
 // rounding).
 #include "tc_common.cuh"
@@ -80,24 +81,28 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
 
   const uint32_t qa = tc::smem_addr(sQ), ka = tc::smem_addr(sK),
                  va = tc::smem_addr(sV), pa = tc::smem_addr(sP);
-  // K and V rows [r0, r0 + 64) into ring slot sl
-  auto stage_kv = [&](int sl, int r0) {
-    if (v16) {
+  // K (or V) rows [r0, r0 + 64) into ring slot sl
+  auto stage_k = [&](int sl, int r0) {
+    if (v16)
       tc::stage_fast<DP, DTC_KEYS, false>(ka + sl * KB, K + (int64_t)r0 * p.st.kn,
                                           p.st.kn, N - r0, d);
+    else
+      tc::stage_kmajor<DP>(sK + sl * KB, K, p.st.kn, r0, DTC_KEYS, N, d, false);
+  };
+  auto stage_v = [&](int sl, int r0) {
+    if (v16)
       tc::stage_fast<DP, DTC_KEYS, true>(va + sl * KB, V + (int64_t)r0 * p.st.vn,
                                          p.st.vn, N - r0, d);
-    } else {
-      tc::stage_kmajor<DP>(sK + sl * KB, K, p.st.kn, r0, DTC_KEYS, N, d, false);
+    else
       tc::stage_mnmajor<DP>(sV + sl * KB, V, p.st.vn, r0, DTC_KEYS, N, d, false);
-    }
   };
   if (v16)
     tc::stage_fast<DP, 128, false>(qa, Q + (int64_t)q0 * p.st.qn, p.st.qn,
                                    N - q0, d);
   else
     tc::stage_kmajor<DP>(sQ, Q, p.st.qn, q0, 128, N, d, false);
-  stage_kv(0, 0);
+  stage_k(0, 0);
+  stage_v(0, 0);
   if (warp == 0) tc::tmem_alloc(&tmem_sh, dtc_tmem_cols<DP>());
   if (threadIdx.x == 0) {
     tc::mbar_init(&mbar_s, 1);
@@ -131,21 +136,21 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
   float l = 0.f;
   bool ok = true;
   const int tiles = cdiv(N, DTC_KEYS);
-  int pv_waited = -1;          // last P V product known complete
   unsigned char* prow = sP + (row >> 3) * PCH * 128 + (row & 7) * 16;
 
+  // Per tile j: S_j was issued ahead of P V_{j-1}, so its wait does not
+  // include that product; P V_{j-1} is awaited only once the weights are in
+  // registers, just before P, the accumulator and V's ring slot are reused.
   for (int j = 0; j < tiles; ++j) {
     const int k0 = j * DTC_KEYS;
-    if (j + 1 < tiles) {
-      // slot (j + 1) & 1 was last read by tile j - 1's products
-      if (j >= 1 && pv_waited < j - 1) {
-        ok &= tc::mbar_wait(&mbar_pv, (uint32_t)((j - 1) & 1));
-        pv_waited = j - 1;
-      }
-      stage_kv((j + 1) & 1, k0 + DTC_KEYS);
-    }
+    const bool more = j + 1 < tiles;
     ok &= tc::mbar_wait(&mbar_s, (uint32_t)(j & 1));
     tc::fence_after_sync();
+    // K slot (j + 1) & 1 last held tile j - 1, whose Q K^T has completed
+    if (more) {
+      stage_k((j + 1) & 1, k0 + DTC_KEYS);
+      cp_async_commit();
+    }
     float s[DTC_KEYS];
     {
       float h[32];
@@ -166,13 +171,6 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
 #pragma unroll
     for (int t = 1; t + 1 < DTC_KEYS; t += 2) mt = max3f(mt, s[t], s[t + 1]);
     mt = fmaxf(mt, s[DTC_KEYS - 1]);
-
-    // P and the accumulator are free once tile j - 1's P V has completed
-    if (j >= 1 && pv_waited < j - 1) {
-      ok &= tc::mbar_wait(&mbar_pv, (uint32_t)((j - 1) & 1));
-      pv_waited = j - 1;
-    }
-    tc::fence_after_sync();
     const bool move = mt > mth;
     float alpha = 1.0f;
     if (move) {
@@ -181,6 +179,21 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
       l *= alpha;
       mref = mn;
       mth = mt + DTC_RESCALE_LOG2 / c2;
+    }
+#pragma unroll
+    for (int t = 0; t < DTC_KEYS; ++t) {
+      s[t] = tc::ex2_approx(fmaf(s[t], c2, -mref));
+      l += s[t];
+    }
+
+    // P V_{j-1} complete: P, the accumulator and V slot (j + 1) & 1 are free
+    if (j >= 1) {
+      ok &= tc::mbar_wait(&mbar_pv, (uint32_t)((j - 1) & 1));
+      tc::fence_after_sync();
+    }
+    if (more) {
+      stage_v((j + 1) & 1, k0 + DTC_KEYS);
+      cp_async_commit();
     }
     // TMEM loads and stores are warp-collective: the whole warp rescales
     // when any lane moved its reference (the others multiply by 1)
@@ -196,26 +209,24 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
     }
 #pragma unroll
     for (int c = 0; c < PCH; ++c) {
-      float e[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        e[u] = tc::ex2_approx(fmaf(s[8 * c + u], c2, -mref));
-        l += e[u];
-      }
       uint4 w;
-      w.x = tc::pack_bf16x2(e[0], e[1]);
-      w.y = tc::pack_bf16x2(e[2], e[3]);
-      w.z = tc::pack_bf16x2(e[4], e[5]);
-      w.w = tc::pack_bf16x2(e[6], e[7]);
+      w.x = tc::pack_bf16x2(s[8 * c], s[8 * c + 1]);
+      w.y = tc::pack_bf16x2(s[8 * c + 2], s[8 * c + 3]);
+      w.z = tc::pack_bf16x2(s[8 * c + 4], s[8 * c + 5]);
+      w.w = tc::pack_bf16x2(s[8 * c + 6], s[8 * c + 7]);
       *reinterpret_cast<uint4*>(prow + c * 128) = w;
     }
-    // K and V of tile j + 1 have landed (this thread's copies); P is written
-    cp_async_wait_all();
+    // this thread's K_{j+1} and V_j have landed (V_{j+1} may be in flight)
+    if (more)
+      cp_async_wait<1>();
+    else
+      cp_async_wait<0>();
     tc::fence_async_smem();
     tc::fence_before_sync();
     __syncthreads();
     tc::fence_after_sync();
     if (threadIdx.x == 0) {
+      if (more) issue_s((j + 1) & 1);
       const int sl = j & 1;
 #pragma unroll
       for (int ks = 0; ks < DTC_KEYS / 16; ++ks)
@@ -224,11 +235,9 @@ __global__ void __launch_bounds__(DTC_THREADS, DP >= 128 ? 2 : 3)
                                    DTC_KEYS * 16),
                      idesc_o, j > 0 || ks > 0);
       tc::mma_commit(&mbar_pv);
-      if (j + 1 < tiles) issue_s((j + 1) & 1);
     }
   }
-  if (pv_waited < tiles - 1)
-    ok &= tc::mbar_wait(&mbar_pv, (uint32_t)((tiles - 1) & 1));
+  ok &= tc::mbar_wait(&mbar_pv, (uint32_t)((tiles - 1) & 1));
   tc::fence_after_sync();
 
   float o[DP];
