@@ -22,7 +22,10 @@
  * reference's eager path, src/kernels/fused_topk_attention.py:390-402):
  *   s[b,i,j] = (q[b,i,:] . k[b,j,:]) * scale, the diagonal j == i excluded;
  *   softmax over the retained peers of row i; out[b,i,:] = sum_j w_ij v[b,j,:].
- * Scores and accumulation are fp32 for both dtypes (bf16 inputs are widened).
+ * Scores and accumulation are fp32. bf16 inputs with N >= 128 form their
+ * scores on the tensor cores (exact bf16 products, fp32 accumulation; the
+ * dense path feeds its softmax weights to P.V as bf16, as the reference's
+ * bf16 kernel does); other bf16 inputs are widened to fp32 on load.
  *
  * Row-count and width limits: 2 <= N, 1 <= d <= 128; `scale` must be positive
  * and finite (TARMAC_ERR_SHAPE otherwise).
@@ -72,7 +75,7 @@ extern "C" {
 
 /* ---- library identity ---------------------------------------------------- */
 /* ABI version of this header; bumped on any signature change. */
-#define TARMAC_ABI_VERSION 1
+#define TARMAC_ABI_VERSION 2
 int tarmac_abi_version(void);
 /* Static text for a status code (never NULL). */
 const char *tarmac_strerror(int status);
@@ -157,6 +160,50 @@ int tarmac_morton_prescore_attention(const void *q, const void *k,
                                      int B, int N, int d, int dtype,
                                      float scale, int topk, int bits,
                                      int64_t *idx_out, void *stream);
+
+/* ---- gradients (training) ------------------------------------------------ */
+/* The reference trains through its eager path and autograd
+ * (src/agents/mappo.py:192-231 topk_gather, 265-292 zorder_k, 361-373 dense);
+ * these entry points give the same gradients for the kernels above.
+ * dout = dL/dout has the layout of q. dq, dk, dv are fp32 [B, N, d]
+ * contiguous and are written in full. */
+
+/* Attention over a fixed peer set: the peers a top-k call retained (its
+ * idx_out), the Morton window, or the indices given to
+ * tarmac_prescore_attention. With s_m = (q_i . k_{j_m}) * scale,
+ * w = softmax(s) and g = dout_i:
+ *   ds_m = w_m (g . v_{j_m} - sum_m' w_m' g . v_{j_m'}),
+ *   dq_i = scale sum_m ds_m k_{j_m},
+ *   dk_j = scale sum_{(i,m): j_m = j} ds_m q_i,
+ *   dv_j = sum_{(i,m): j_m = j} w_m g.
+ * The selection carries no gradient (torch.topk's backward scatters only into
+ * the selected entries). dk and dv are zeroed on the stream, then
+ * accumulated with atomic adds, so their summation order is not fixed. A row
+ * naming an index outside [0, N) gets a NaN dq row and adds nothing to dk/dv.
+ * strides: 8 int64 { q_b, q_n, k_b, k_n, v_b, v_n, dout_b, dout_n } or NULL.
+ * idx: contiguous [B, N, kk], int64 when idx_is_i64 else int32. */
+int tarmac_gather_attention_backward(const void *q, const void *k,
+                                     const void *v, const void *dout,
+                                     const int64_t *strides, const void *idx,
+                                     int idx_is_i64, int kk, int B, int N,
+                                     int d, int dtype, float scale, float *dq,
+                                     float *dk, float *dv, void *stream);
+
+/* Dense masked-diagonal attention (tarmac_dense_attention). With
+ * P = softmax(Q K^T scale) over j != i, `out` the forward output and
+ * D_i = dout_i . out_i:
+ *   dq_i = scale sum_j P_ij (dout_i . v_j - D_i) k_j,
+ *   dk_j = scale sum_i P_ij (dout_i . v_j - D_i) q_i,
+ *   dv_j = sum_i P_ij dout_i.
+ * P is recomputed, never stored; deterministic. work: fp32 [2, B, N] scratch
+ * (row log-sum-exp, then D). strides: 10 int64
+ * { q_b, q_n, k_b, k_n, v_b, v_n, out_b, out_n, dout_b, dout_n } or NULL. */
+int tarmac_dense_attention_backward(const void *q, const void *k,
+                                    const void *v, const void *out,
+                                    const void *dout, const int64_t *strides,
+                                    int B, int N, int d, int dtype, float scale,
+                                    float *dq, float *dk, float *dv,
+                                    float *work, void *stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

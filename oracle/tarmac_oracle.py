@@ -213,6 +213,60 @@ def prescore_attention(q, k, v, idx):
     return out
 
 
+# ---------------------------------------------------------------------------
+# gradients: what autograd forms through the reference's eager path
+# ---------------------------------------------------------------------------
+
+def gather_attention_grad(q, k, v, idx, g, scale: float | None = None):
+    """Gradients (dq, dk, dv) of attention over a fixed peer set, float64.
+
+    The eager path gathers the selected rows and contracts
+    (src/agents/mappo.py:211-222 topk_gather, 279-286 zorder_k;
+    prescore_selection.py:442-453): s = q.k_j * scale, w = softmax(s),
+    out = sum w v_j. The indices come from topk / the Morton selector and
+    carry no gradient, so autograd's result is the chain rule through
+    gather, softmax and the two contractions, with scatter-adds into dk, dv.
+    """
+    B, N, d = q.shape
+    sc = 1.0 / np.sqrt(d) if scale is None else float(scale)
+    idx = np.asarray(idx, dtype=np.int64)
+    q64, k64, v64, g64 = (np.asarray(t, dtype=np.float64) for t in (q, k, v, g))
+    bi = np.arange(B)[:, None, None]
+    kg, vg = k64[bi, idx], v64[bi, idx]              # [B, N, kk, d]
+    s = np.einsum("bnd,bnjd->bnj", q64, kg) * sc
+    w = np.exp(s - s.max(-1, keepdims=True))
+    w /= w.sum(-1, keepdims=True)
+    dw = np.einsum("bnd,bnjd->bnj", g64, vg)
+    ds = w * (dw - (w * dw).sum(-1, keepdims=True))
+    dq = sc * np.einsum("bnj,bnjd->bnd", ds, kg)
+    dk = np.zeros_like(k64)
+    dv = np.zeros_like(v64)
+    bb = np.broadcast_to(bi, idx.shape)
+    np.add.at(dk, (bb, idx), sc * ds[..., None] * q64[:, :, None, :])
+    np.add.at(dv, (bb, idx), w[..., None] * g64[:, :, None, :])
+    return dq, dk, dv
+
+
+def dense_attention_grad(q, k, v, g, scale: float | None = None):
+    """Gradients (dq, dk, dv) of dense masked-diagonal attention, float64:
+    the chain rule through the eager path's matmul, masked softmax and matmul
+    (src/agents/mappo.py:361-373)."""
+    B, N, d = q.shape
+    sc = 1.0 / np.sqrt(d) if scale is None else float(scale)
+    q64, k64, v64, g64 = (np.asarray(t, dtype=np.float64) for t in (q, k, v, g))
+    s = np.einsum("bid,bjd->bij", q64, k64) * sc
+    s[:, np.arange(N), np.arange(N)] = -np.inf
+    p = np.exp(s - s.max(-1, keepdims=True))
+    p /= p.sum(-1, keepdims=True)
+    out = np.einsum("bij,bjd->bid", p, v64)
+    dp = np.einsum("bid,bjd->bij", g64, v64)
+    dsc = p * (dp - (g64 * out).sum(-1)[..., None])
+    dq = sc * np.einsum("bij,bjd->bid", dsc, k64)
+    dk = sc * np.einsum("bij,bid->bjd", dsc, q64)
+    dv = np.einsum("bij,bid->bjd", p, g64)
+    return dq, dk, dv
+
+
 _SPREAD = ((8, 0x00FF00FF), (4, 0x0F0F0F0F), (2, 0x33333333), (1, 0x55555555))
 
 

@@ -5,6 +5,7 @@
 // caller's stream. No memory is allocated and no stream is synchronised.
 #include <math.h>
 
+#include "backward.cuh"
 #include "common.cuh"
 #include "topk_chunk.cuh"
 
@@ -101,6 +102,57 @@ static int fill_params(AttnParams& p, const void* q, const void* k,
   p.qscale = pow2 ? scale : 1.0f;
   p.post_scale = pow2 ? 1.0f : scale;
   p.idx_out = nullptr;
+  p.vec = vec ? 1 : 0;
+  return TARMAC_OK;
+}
+
+// Validate the gradient operand block (q, k, v, dout and, for dense, out);
+// strides holds 8 (gather) or 10 (dense) int64 element strides, or NULL.
+static int fill_bwd(BwdParams& p, const void* q, const void* k, const void* v,
+                    const void* out, const void* dout, const int64_t* strides,
+                    int nstrides, int B, int N, int d, int dtype, float scale,
+                    float* dq, float* dk, float* dv) {
+  if (!q || !k || !v || !dout || !dq || !dk || !dv) return TARMAC_ERR_NULL;
+  if (nstrides == 10 && !out) return TARMAC_ERR_NULL;
+  if (dtype != TARMAC_F32 && dtype != TARMAC_BF16) return TARMAC_ERR_DTYPE;
+  if (B < 0 || N < 2 || d < 1 || d > MAX_D) return TARMAC_ERR_SHAPE;
+  if (!(scale > 0.f) || isinf(scale)) return TARMAC_ERR_SHAPE;
+  const int es = elem_size(dtype);
+  if (!aligned(q, es) || !aligned(k, es) || !aligned(v, es) ||
+      !aligned(dout, es) || (out && !aligned(out, es)))
+    return TARMAC_ERR_ALIGN;
+  if (!aligned(dq, 4) || !aligned(dk, 4) || !aligned(dv, 4))
+    return TARMAC_ERR_ALIGN;
+  int64_t st[10];
+  const int64_t rs = d, bs = (int64_t)N * d;
+  for (int i = 0; i < 10; i += 2) {
+    st[i] = bs;
+    st[i + 1] = rs;
+  }
+  if (strides) {
+    if (nstrides == 10) {
+      for (int i = 0; i < 10; ++i) st[i] = strides[i];
+    } else {  // q, k, v, dout: dout's pair goes to the last slot
+      for (int i = 0; i < 6; ++i) st[i] = strides[i];
+      st[8] = strides[6];
+      st[9] = strides[7];
+    }
+  }
+  const uintptr_t va = (uintptr_t)(4 * es);
+  bool vec = (d % 4) == 0 && aligned(q, va) && aligned(k, va) &&
+             aligned(v, va) && aligned(dout, va) && (!out || aligned(out, va));
+  for (int i = 0; i < 10; ++i) vec = vec && (st[i] % 4) == 0;
+  p.q = q; p.k = k; p.v = v; p.o = out; p.g = dout;
+  p.qb = st[0]; p.qn = st[1]; p.kb = st[2]; p.kn = st[3];
+  p.vb = st[4]; p.vn = st[5]; p.ob = st[6]; p.on = st[7];
+  p.gb = st[8]; p.gn = st[9];
+  p.B = B; p.N = N; p.d = d;
+  p.scale = scale;
+  p.dq = dq; p.dk = dk; p.dv = dv;
+  p.work = nullptr;
+  p.idx = nullptr;
+  p.idx_i64 = 0;
+  p.kk = 0;
   p.vec = vec ? 1 : 0;
   return TARMAC_OK;
 }
@@ -245,6 +297,45 @@ int tarmac_morton_prescore_attention(const void* q, const void* k,
   if (B == 0) return TARMAC_OK;
   return launch_status(launch_morton_prescore(p, dtype, pos, bits, idx_out,
                                               (cudaStream_t)stream));
+}
+
+int tarmac_gather_attention_backward(const void* q, const void* k,
+                                     const void* v, const void* dout,
+                                     const int64_t* strides, const void* idx,
+                                     int idx_is_i64, int kk, int B, int N,
+                                     int d, int dtype, float scale, float* dq,
+                                     float* dk, float* dv, void* stream) {
+  BwdParams p;
+  int st = fill_bwd(p, q, k, v, nullptr, dout, strides, 8, B, N, d, dtype,
+                    scale, dq, dk, dv);
+  if (st != TARMAC_OK) return st;
+  if (!idx) return TARMAC_ERR_NULL;
+  if (kk < 1) return TARMAC_ERR_TOPK;
+  if (!aligned(idx, idx_is_i64 ? 8 : 4)) return TARMAC_ERR_ALIGN;
+  p.idx = idx;
+  p.idx_i64 = idx_is_i64 != 0;
+  p.kk = kk;
+  if (B == 0) return TARMAC_OK;
+  return launch_status(
+      launch_gather_bwd(p, dtype == TARMAC_BF16, (cudaStream_t)stream));
+}
+
+int tarmac_dense_attention_backward(const void* q, const void* k,
+                                    const void* v, const void* out,
+                                    const void* dout, const int64_t* strides,
+                                    int B, int N, int d, int dtype, float scale,
+                                    float* dq, float* dk, float* dv,
+                                    float* work, void* stream) {
+  BwdParams p;
+  int st = fill_bwd(p, q, k, v, out, dout, strides, 10, B, N, d, dtype, scale,
+                    dq, dk, dv);
+  if (st != TARMAC_OK) return st;
+  if (!work) return TARMAC_ERR_NULL;
+  if (!aligned(work, 4)) return TARMAC_ERR_ALIGN;
+  p.work = work;
+  if (B == 0) return TARMAC_OK;
+  return launch_status(
+      launch_dense_bwd(p, dtype == TARMAC_BF16, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -16,9 +16,10 @@ and forward signature ``forward(x, pos=None) -> (msg, info)``
                             selected peers, 10-bit codes (mappo.py:265-292)
 
 The q, k, v chunks of the qkv output are passed to the kernels as strided
-views (no copies). The kernels are forward-only, like the reference's Triton
-kernels (scripts/bench_attention_core.py:172-176): a backward pass through the
-attention core raises NotImplementedError. The ``random_k``, ``entmax`` and
+views (no copies). Training works: the attention core's backward runs the
+gradient kernels (tarmac_b200.autograd), giving the gradients autograd forms
+through the reference's eager path (the peer selection carries none).
+Gradients of the top-k modes need k <= 8. The ``random_k``, ``entmax`` and
 ``adaptive_topk`` study arms and the MAPPO actor/critic are outside this build.
 The weight-based diagnostics of ``collect_info`` (attention entropy) need the
 weight matrix, which the fused kernels never form; ``info`` carries
@@ -34,7 +35,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from tarmac_b200 import ops
+from tarmac_b200 import autograd as tgrad
 
 #: Slice of a simple_spread observation holding the agent's own position
 #: (mappo.py:24-28).
@@ -60,19 +61,6 @@ class MAPPOConfig:
 def _ortho_init(layer: nn.Linear, gain: float = float(np.sqrt(2.0))) -> None:
     nn.init.orthogonal_(layer.weight, gain=gain)
     nn.init.zeros_(layer.bias)
-
-
-class _ForwardOnly(torch.autograd.Function):
-    """Runs a kernel launcher; its backward is not implemented."""
-
-    @staticmethod
-    def forward(ctx, fn, q, k, v, *extra):
-        return fn(q, k, v, *extra)
-
-    @staticmethod
-    def backward(ctx, *grads):
-        raise NotImplementedError(
-            "the tarmac_b200 attention-core kernels are forward-only")
 
 
 class AttentionComm(nn.Module):
@@ -110,16 +98,13 @@ class AttentionComm(nn.Module):
             if pos is None:
                 raise ValueError("attn_mode='zorder_k' needs agent positions")
             k_eff = self._k_eff(N)
-            msg = _ForwardOnly.apply(
-                lambda a, b, c, p: ops.morton_prescore_attention(
-                    a, b, c, p, k_eff, MORTON_BITS), q, k, v, pos.float())
+            msg = tgrad.morton_prescore_attention(q, k, v, pos.float(), k_eff,
+                                                  MORTON_BITS)
             info["effective_k"] = float(k_eff)
         elif mode in ("dense", "dense_sdpa"):
-            msg = _ForwardOnly.apply(ops.dense_attention, q, k, v)
+            msg = tgrad.dense_attention(q, k, v)
         else:
             k_eff = self._k_eff(N)
-            msg = _ForwardOnly.apply(
-                lambda a, b, c: ops.topk_attention(a, b, c, k_eff, "argmax"),
-                q, k, v)
+            msg = tgrad.topk_attention(q, k, v, k_eff, "argmax")
             info["effective_k"] = float(k_eff)
         return self.proj(F.gelu(msg)), info

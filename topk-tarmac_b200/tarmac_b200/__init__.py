@@ -6,6 +6,8 @@ Host-side package over the C ABI of ``include/tarmac_b200.h``
 * :mod:`tarmac_b200.ops` — torch-facing launchers (dense, fused top-k in three
   tie modes, streaming top-k, attention over a given peer set, Morton codes,
   Morton window selection, fused Morton selection + attention);
+* :mod:`tarmac_b200.autograd` — differentiable forms (torch.autograd.Function)
+  whose backward runs the gradient kernels;
 * :mod:`tarmac_b200._lib` — the ctypes binding itself.
 
 The drop-in modules with the reference's import paths (``src.kernels.*``,
@@ -14,10 +16,10 @@ The drop-in modules with the reference's import paths (``src.kernels.*``,
 
 from __future__ import annotations
 
-from . import _lib, ops  # noqa: F401
+from . import _lib, autograd, ops  # noqa: F401
 from ._lib import TarmacError, lib  # noqa: F401
 
-__all__ = ["ops", "lib", "TarmacError", "load"]
+__all__ = ["ops", "autograd", "lib", "TarmacError", "load"]
 
 
 def load():

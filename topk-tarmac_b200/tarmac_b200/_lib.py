@@ -14,7 +14,7 @@ from ctypes import c_char_p, c_float, c_int, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libtarmac_b200.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # status codes (include/tarmac_b200.h)
 OK = 0
@@ -61,6 +61,14 @@ SIGNATURES: dict[str, tuple] = {
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
         c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_void_p,
         c_void_p]),
+    "tarmac_gather_attention_backward": (c_int, [
+        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+        c_int, c_int, c_int, c_int, c_int, c_int, c_float,
+        c_void_p, c_void_p, c_void_p, c_void_p]),
+    "tarmac_dense_attention_backward": (c_int, [
+        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+        c_int, c_int, c_int, c_int, c_float,
+        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _LOCK = threading.Lock()

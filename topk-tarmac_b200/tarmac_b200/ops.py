@@ -214,3 +214,74 @@ def morton_prescore_attention(q: torch.Tensor, k: torch.Tensor,
                   B, N, d, _DTYPES[q.dtype], _scale(d, scale), int(topk),
                   int(bits), _ptr(idx), _stream(q.device))
     return (out, idx) if return_indices else out
+
+
+# ---------------------------------------------------------------------------
+# gradients (training path)
+# ---------------------------------------------------------------------------
+
+def _strides_n(*ts) -> ctypes.Array:
+    vals = []
+    for t in ts:
+        vals += [t.stride(0), t.stride(1)]
+    return (ctypes.c_int64 * len(vals))(*vals)
+
+
+def gather_attention_backward(q: torch.Tensor, k: torch.Tensor,
+                              v: torch.Tensor, dout: torch.Tensor,
+                              idx: torch.Tensor, scale: float | None = None):
+    """Gradients (dq, dk, dv), fp32 [B, N, d], of attention over the fixed
+    peer set ``idx`` ([B, N, kk], int32 or int64): the peers a top-k call
+    retained, the Morton window, or given indices. The selection carries no
+    gradient. dk and dv accumulate with atomic adds (summation order not
+    fixed)."""
+    q, k, v = _check_qkv(q, k, v)
+    dout = _unit_inner(dout)
+    B, N, d = q.shape
+    if dout.shape != q.shape or dout.device != q.device:
+        raise ValueError("dout must match q's shape and device")
+    if dout.dtype != q.dtype:
+        dout = dout.to(q.dtype)
+    if idx.dim() != 3 or tuple(idx.shape[:2]) != (B, N):
+        raise ValueError(f"idx must be [B, N, kk]; got {tuple(idx.shape)}")
+    if idx.dtype not in (torch.int64, torch.int32):
+        raise TypeError(f"idx must be int64 or int32; got {idx.dtype}")
+    idx = idx.contiguous()
+    dq = torch.empty((B, N, d), device=q.device, dtype=torch.float32)
+    dk = torch.empty_like(dq)
+    dv = torch.empty_like(dq)
+    strides = _strides_n(q, k, v, dout)
+    with torch.cuda.device(q.device):
+        _lib.call("tarmac_gather_attention_backward", _ptr(q), _ptr(k),
+                  _ptr(v), _ptr(dout), ctypes.addressof(strides), _ptr(idx),
+                  int(idx.dtype == torch.int64), idx.shape[-1], B, N, d,
+                  _DTYPES[q.dtype], _scale(d, scale), _ptr(dq), _ptr(dk),
+                  _ptr(dv), _stream(q.device))
+    return dq, dk, dv
+
+
+def dense_attention_backward(q: torch.Tensor, k: torch.Tensor,
+                             v: torch.Tensor, out: torch.Tensor,
+                             dout: torch.Tensor, scale: float | None = None):
+    """Gradients (dq, dk, dv), fp32 [B, N, d], of dense masked-diagonal
+    attention given its forward output ``out``. P is recomputed, not stored;
+    deterministic."""
+    q, k, v = _check_qkv(q, k, v)
+    out, dout = _unit_inner(out), _unit_inner(dout)
+    B, N, d = q.shape
+    for t, name in ((out, "out"), (dout, "dout")):
+        if t.shape != q.shape or t.device != q.device:
+            raise ValueError(f"{name} must match q's shape and device")
+    out = out.to(q.dtype)
+    dout = dout.to(q.dtype)
+    dq = torch.empty((B, N, d), device=q.device, dtype=torch.float32)
+    dk = torch.empty_like(dq)
+    dv = torch.empty_like(dq)
+    work = torch.empty((2, B, N), device=q.device, dtype=torch.float32)
+    strides = _strides_n(q, k, v, out, dout)
+    with torch.cuda.device(q.device):
+        _lib.call("tarmac_dense_attention_backward", _ptr(q), _ptr(k), _ptr(v),
+                  _ptr(out), _ptr(dout), ctypes.addressof(strides), B, N, d,
+                  _DTYPES[q.dtype], _scale(d, scale), _ptr(dq), _ptr(dk),
+                  _ptr(dv), _ptr(work), _stream(q.device))
+    return dq, dk, dv
