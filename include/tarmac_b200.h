@@ -161,6 +161,36 @@ int tarmac_morton_prescore_attention(const void *q, const void *k,
                                      float scale, int topk, int bits,
                                      int64_t *idx_out, void *stream);
 
+/* ---- positional and random selectors ------------------------------------- */
+/* Exact k nearest peers of every agent by Euclidean distance (squared
+ * distance dx^2 + dy^2 in fp32, self excluded), listed by increasing
+ * (distance, index): the lowest index wins an exact tie. pos: fp32
+ * [B, N, 2] contiguous; idx_out: int64 [B, N, k]. 2 <= N <= 8192,
+ * 1 <= k <= min(N - 1, 32). Replaces select_radius_knn
+ * (src/kernels/prescore_selection.py:35-42). */
+int tarmac_knn_select(const float *pos, int B, int N, int k, int64_t *idx_out,
+                      void *stream);
+
+/* Grid kNN: the k nearest among the 3 x 3 grid cells around each agent, with
+ * the reference's grid side G = floor(sqrt(N / max(2, k))) and per-cell
+ * capacity M = floor(mean + 3 sqrt(mean) + 2) (mean = N / G^2); each of the
+ * three column runs of the 3 x 3 block is cut at 3M agents in cell order
+ * (cells sorted stably: equal cells keep agent order). When 9M >= N the exact
+ * selector runs instead, as in the reference; an agent whose runs hold fewer
+ * than k candidates takes its exact k nearest. Same layout and limits as
+ * tarmac_knn_select. Replaces select_grid_knn
+ * (src/kernels/prescore_selection.py:81-162). */
+int tarmac_grid_knn_select(const float *pos, int B, int N, int k,
+                           int64_t *idx_out, void *stream);
+
+/* k distinct peers per agent, uniform over the k-subsets of the other N - 1
+ * agents, from a Philox stream keyed by (seed, row, offset): the selection
+ * rule of the random_k arm (src/agents/mappo.py:233-263). idx_out: int64
+ * [B, N, k], 1 <= k <= N - 1. */
+int tarmac_random_select(int B, int N, int k, unsigned long long seed,
+                         unsigned long long offset, int64_t *idx_out,
+                         void *stream);
+
 /* ---- gradients (training) ------------------------------------------------ */
 /* The reference trains through its eager path and autograd
  * (src/agents/mappo.py:192-231 topk_gather, 265-292 zorder_k, 361-373 dense);

@@ -267,6 +267,115 @@ def dense_attention_grad(q, k, v, g, scale: float | None = None):
     return dq, dk, dv
 
 
+# ---------------------------------------------------------------------------
+# positional selectors
+# ---------------------------------------------------------------------------
+
+def _dist2(pi: np.ndarray, pj: np.ndarray) -> np.ndarray:
+    """fp32 squared distance, each step rounded (no fused multiply-add)."""
+    dx = (pj[..., 0] - pi[..., 0]).astype(np.float32)
+    dy = (pj[..., 1] - pi[..., 1]).astype(np.float32)
+    return (dx * dx).astype(np.float32) + (dy * dy).astype(np.float32)
+
+
+def knn_exact(pos: np.ndarray, k: int) -> np.ndarray:
+    """k nearest peers, self excluded, by increasing (distance, index);
+    int64 [B, N, k].
+
+    select_radius_knn (src/kernels/prescore_selection.py:35-42) ranks
+    cdist(pos, pos) with the diagonal at +inf and keeps the k smallest; the
+    squared distance has the same order, and exact ties go to the lower index.
+    """
+    pos = np.asarray(pos, dtype=np.float32)
+    B, N, _ = pos.shape
+    out = np.empty((B, N, k), dtype=np.int64)
+    for b in range(B):
+        d2 = _dist2(pos[b][:, None, :], pos[b][None, :, :])
+        d2[np.arange(N), np.arange(N)] = np.inf
+        # candidates: every peer at or below the k-th smallest distance (all
+        # of a tie at the boundary), then the first k by (distance, index)
+        kth = np.partition(d2, k - 1, axis=-1)[:, k - 1:k]
+        rows, cols = np.nonzero(d2 <= kth)
+        order = np.lexsort((cols, d2[rows, cols], rows))
+        rows, cols = rows[order], cols[order]
+        first = np.searchsorted(rows, np.arange(N))
+        out[b] = cols[first[:, None] + np.arange(k)[None, :]]
+    return out
+
+
+def knn_ambiguous(pos: np.ndarray, k: int, tol: float = 1e-6) -> np.ndarray:
+    """Rows whose k-th and (k+1)-th squared distances differ by less than
+    ``tol``: rounding of a distance evaluation (the reference's cdist uses a
+    matrix-product form for larger N) may order them either way."""
+    pos = np.asarray(pos, dtype=np.float64)
+    B, N, _ = pos.shape
+    res = np.zeros((B, N), dtype=bool)
+    if k >= N - 1:
+        return res
+    for b in range(B):
+        d2 = ((pos[b][:, None, :] - pos[b][None, :, :]) ** 2).sum(-1)
+        d2[np.arange(N), np.arange(N)] = np.inf
+        srt = np.sort(d2, axis=-1)
+        res[b] = (srt[:, k] - srt[:, k - 1]) < tol
+    return res
+
+
+def grid_knn_shape(N: int, k: int) -> tuple[int, int]:
+    """Grid side and per-cell capacity (prescore_selection.py:81-97)."""
+    occ = max(2, k)
+    G = max(1, int((N / occ) ** 0.5))
+    mean = N / (G * G)
+    return G, int(mean + 3 * mean ** 0.5 + 2)
+
+
+def grid_knn(pos: np.ndarray, k: int) -> np.ndarray:
+    """Grid kNN, int64 [B, N, k] by increasing (distance, index).
+
+    select_grid_knn (src/kernels/prescore_selection.py:103-162): cells of a
+    G x G grid over the episode's bounding box (normalise, scale by G,
+    truncate, clamp), agents sorted by cell id x*G + y (stably: equal cells
+    keep agent order), and for each agent the three sorted runs from cell
+    (x', max(y-1, 0)) to the end of cell (x', min(y+1, G-1)) for
+    x' = x-1..x+1, each cut at 3M entries; the k nearest among them. The
+    exact selector when 9M >= N; an agent with fewer than k candidates takes
+    its exact k nearest.
+    """
+    pos = np.asarray(pos, dtype=np.float32)
+    B, N, _ = pos.shape
+    G, M = grid_knn_shape(N, k)
+    L = 3 * M
+    if 3 * L >= N:
+        return knn_exact(pos, k)
+    out = np.empty((B, N, k), dtype=np.int64)
+    exact = knn_exact(pos, k)
+    for b in range(B):
+        p = pos[b]
+        lo = p.min(0)
+        span = np.maximum((p.max(0) - lo).astype(np.float32), np.float32(1e-6))
+        g = (((p - lo).astype(np.float32) / span).astype(np.float32)
+             * np.float32(G)).astype(np.float32)
+        cxy = np.clip(np.trunc(g).astype(np.int64), 0, G - 1)
+        cell = cxy[:, 0] * G + cxy[:, 1]
+        order = np.argsort(cell, kind="stable")
+        start = np.searchsorted(cell[order], np.arange(G * G + 1), side="left")
+        for i in range(N):
+            x, y = cxy[i]
+            cand = []
+            for xx in (x - 1, x, x + 1):
+                if xx < 0 or xx >= G:
+                    continue
+                s_lo = start[xx * G + max(y - 1, 0)]
+                s_hi = min(start[xx * G + min(y + 1, G - 1) + 1], s_lo + L)
+                cand.extend(int(j) for j in order[s_lo:s_hi] if j != i)
+            if len(cand) < k:
+                out[b, i] = exact[b, i]
+                continue
+            cand = np.array(sorted(cand))
+            d2 = _dist2(p[i][None, :], p[cand])
+            out[b, i] = cand[np.argsort(d2, kind="stable")[:k]]
+    return out
+
+
 _SPREAD = ((8, 0x00FF00FF), (4, 0x0F0F0F0F), (2, 0x33333333), (1, 0x55555555))
 
 

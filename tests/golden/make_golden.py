@@ -7,7 +7,9 @@ on the CPU, and stores inputs and outputs as ``tests/golden/*.npz``:
   (src/kernels/fused_topk_attention.py:390-402), ``dense_unfused``
   (scripts/bench_attention_core.py:74-75), ``_morton_code`` and
   ``select_morton_window`` (src/kernels/prescore_selection.py:320-342),
-  ``prescore_attention`` (src/kernels/prescore_selection.py:442-453);
+  ``prescore_attention`` (src/kernels/prescore_selection.py:442-453),
+  ``select_radius_knn``, ``select_grid_knn``, ``grid_knn_recall``
+  (src/kernels/prescore_selection.py:35-170);
 * the reference's Triton kernels run by Triton's CPU interpreter
   (``TRITON_INTERPRET=1``), which pin the kernel-specific tie rules:
   ``fused_topk_attention_tiled`` (lowest index), ``fused_topk_attention_sort``
@@ -54,7 +56,14 @@ def _qkv(gen, B, N, d):
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--reference", required=True, type=Path)
+    ap.add_argument("--only", default=None,
+                    help="comma-separated fixture groups to (re)write: "
+                         "topk,dense,morton,selectors (default: all)")
     args = ap.parse_args()
+    only = set(args.only.split(",")) if args.only else None
+
+    def want(group):
+        return only is None or group in only
     fta, fda, fpa, ps, sta, bac = _setup(args.reference.resolve())
     import numpy as np
     import torch
@@ -66,6 +75,20 @@ def main() -> int:
         print("wrote", name, {k: v.shape for k, v in out.items()})
 
     # -- fused top-k: eager reference + interpreted kernels ------------------
+    if want("topk"):
+        _topk_fixtures(fta, sta, save)
+    if want("dense"):
+        _dense_fixtures(fda, bac, save)
+    if want("morton"):
+        _morton_fixtures(ps, fpa, save)
+    if want("selectors"):
+        _selector_fixtures(ps, save)
+    return 0
+
+
+def _topk_fixtures(fta, sta, save):
+    import numpy as np
+    import torch
     cases = [("topk_c1", 8, 6, 16, (1, 2, 4)),
              ("topk_n40", 4, 40, 16, (1, 2, 4, 7)),
              ("topk_n64_d32", 2, 64, 32, (1, 3, 8)),
@@ -116,7 +139,10 @@ def main() -> int:
         rec[f"eager_k{kk}"] = fta.reference_topk_attention(q, k, v, kk)
     save("topk_modes", **rec)
 
-    # -- dense ----------------------------------------------------------------
+
+
+def _dense_fixtures(fda, bac, save):
+    import torch
     for name, B, N, d in (("dense_n40", 4, 40, 16), ("dense_c1", 8, 6, 16),
                           ("dense_n70_d32", 2, 70, 32)):
         gen = torch.Generator().manual_seed(1234 + 7 * N + d)
@@ -126,7 +152,11 @@ def main() -> int:
              eager=bac.dense_unfused(q, k, v, eye, N - 1),
              flash=fda.fused_dense_attention(q, k, v))
 
-    # -- Morton codes, window selection, prescore attention ------------------
+
+
+def _morton_fixtures(ps, fpa, save):
+    import numpy as np
+    import torch
     gen = torch.Generator().manual_seed(4242 + 50)
     B, N, d = 6, 50, 16
     q, k, v = _qkv(gen, B, N, d)
@@ -153,7 +183,25 @@ def main() -> int:
     save("morton_edge", pos=pos, code10=ps._morton_code(pos),
          code16=ps._morton_code(pos, bits=16),
          code4=ps._morton_code(pos, bits=4))
-    return 0
+
+
+def _selector_fixtures(ps, save):
+    """select_radius_knn, select_grid_knn (grid path at N >= 600, the exact
+    fallback at N = 50) and grid_knn_recall on seeded uniform positions."""
+    import numpy as np
+    import torch
+    for name, B, N, ks in (("knn_n50", 4, 50, (1, 2, 5)),
+                           ("knn_n600", 3, 600, (2, 4)),
+                           ("knn_n3000", 1, 3000, (2,))):
+        gen = torch.Generator().manual_seed(4242 + N)
+        pos = torch.rand(B, N, 2, generator=gen)
+        rec = {"pos": pos, "ks": np.array(ks)}
+        for kk in ks:
+            rec[f"radius_k{kk}"] = ps.select_radius_knn(pos, kk)
+            rec[f"grid_k{kk}"] = ps.select_grid_knn(pos, kk)
+            rec[f"shape_k{kk}"] = np.array(ps.grid_knn_shape(N, kk))
+            rec[f"recall_k{kk}"] = np.array(ps.grid_knn_recall(pos, kk))
+        save(name, **rec)
 
 
 if __name__ == "__main__":

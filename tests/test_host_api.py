@@ -9,6 +9,8 @@ import inspect
 import pytest
 import torch
 
+import oracle
+
 from src.agents import mappo
 from src.kernels import fused_dense_attention as fda
 from src.kernels import fused_prescore_attention as fpa
@@ -67,14 +69,15 @@ def test_cpu_tensors_fail_loudly():
         ps.select_morton_window(torch.zeros(2, 8, 2), 2)
 
 
-def test_out_of_scope_selectors_raise():
+def test_selectors_need_cuda_and_ledger_is_out_of_scope():
     pos = torch.zeros(1, 8, 2)
     for fn in (ps.select_radius_knn, ps.select_grid_knn, ps.grid_knn_recall):
-        with pytest.raises(NotImplementedError):
+        with pytest.raises(RuntimeError, match="CUDA"):
             fn(pos, 2)
     with pytest.raises(NotImplementedError):
         ps.analytic_flops("morton_window", 1, 8, 16, 2)
     assert ps.grid_knn_shape(512, 2) == (16, 8)
+    assert ps.grid_knn_shape(600, 2) == oracle.grid_knn_shape(600, 2)
 
 
 def test_tuned_cfg_absent_table_is_none():

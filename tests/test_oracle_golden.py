@@ -169,3 +169,24 @@ def test_ambiguity_classifier_flags_near_ties_only():
         near = set(top[i]) == {2, 3}
         if near:
             assert amb[0, i]
+
+
+@pytest.mark.parametrize("name", ["knn_n50", "knn_n600", "knn_n3000"])
+def test_knn_selectors_match_reference(golden, name):
+    """select_radius_knn and select_grid_knn (exact fallback at N=50, grid
+    path at N=600 and 3000) against the reference's own outputs: the same
+    peer set on every row whose k-th and (k+1)-th distances are not within
+    rounding of each other."""
+    g = golden(name)
+    pos = g["pos"]
+    for kk in g["ks"]:
+        kk = int(kk)
+        amb = oracle.knn_ambiguous(pos, kk)
+        ok = ~amb
+        assert tuple(g[f"shape_k{kk}"]) == oracle.grid_knn_shape(pos.shape[1], kk)
+        np.testing.assert_array_equal(
+            np.sort(oracle.knn_exact(pos, kk), -1)[ok],
+            np.sort(g[f"radius_k{kk}"], -1)[ok])
+        np.testing.assert_array_equal(
+            np.sort(oracle.grid_knn(pos, kk), -1)[ok],
+            np.sort(g[f"grid_k{kk}"], -1)[ok])

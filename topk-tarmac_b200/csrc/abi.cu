@@ -48,6 +48,13 @@ cudaError_t launch_morton_code(const float* pos, int B, int N, int bits,
                                int64_t* out, cudaStream_t s);
 cudaError_t launch_morton_select(const float* pos, int B, int N, int k,
                                  int bits, int64_t* idx_out, cudaStream_t s);
+cudaError_t launch_knn_select(const float* pos, int B, int N, int k,
+                              int64_t* out, cudaStream_t s);
+cudaError_t launch_grid_knn_select(const float* pos, int B, int N, int k,
+                                   int64_t* out, cudaStream_t s);
+cudaError_t launch_random_select(int B, int N, int k, unsigned long long seed,
+                                 unsigned long long offset, int64_t* out,
+                                 cudaStream_t s);
 cudaError_t launch_morton_prescore(const AttnParams& p, int dtype,
                                    const float* pos, int bits,
                                    int64_t* idx_out, cudaStream_t s);
@@ -57,6 +64,8 @@ constexpr int RESIDENT_MAX_N = 1024;
 constexpr int STREAM_MAX_K = 8;
 constexpr int REGISTER_MAX_K = 8;
 constexpr int MORTON_MAX_N = 4096;
+constexpr int SELECT_MAX_N = 8192;
+constexpr int SELECT_MAX_K = 32;
 
 static bool aligned(const void* ptr, uintptr_t a) {
   return (reinterpret_cast<uintptr_t>(ptr) & (a - 1)) == 0;
@@ -336,6 +345,44 @@ int tarmac_dense_attention_backward(const void* q, const void* k,
   if (B == 0) return TARMAC_OK;
   return launch_status(
       launch_dense_bwd(p, dtype == TARMAC_BF16, (cudaStream_t)stream));
+}
+
+static int check_select(const float* pos, int B, int N, int k,
+                        const int64_t* idx_out) {
+  if (!pos || !idx_out) return TARMAC_ERR_NULL;
+  if (B < 0 || N < 2) return TARMAC_ERR_SHAPE;
+  if (N > SELECT_MAX_N) return TARMAC_ERR_N_TOO_LARGE;
+  if (k < 1 || k > N - 1 || k > SELECT_MAX_K) return TARMAC_ERR_TOPK;
+  if (!aligned(pos, 8) || !aligned(idx_out, 8)) return TARMAC_ERR_ALIGN;
+  return TARMAC_OK;
+}
+
+int tarmac_knn_select(const float* pos, int B, int N, int k, int64_t* idx_out,
+                      void* stream) {
+  const int st = check_select(pos, B, N, k, idx_out);
+  if (st != TARMAC_OK || B == 0) return st;
+  return launch_status(
+      launch_knn_select(pos, B, N, k, idx_out, (cudaStream_t)stream));
+}
+
+int tarmac_grid_knn_select(const float* pos, int B, int N, int k,
+                           int64_t* idx_out, void* stream) {
+  const int st = check_select(pos, B, N, k, idx_out);
+  if (st != TARMAC_OK || B == 0) return st;
+  return launch_status(
+      launch_grid_knn_select(pos, B, N, k, idx_out, (cudaStream_t)stream));
+}
+
+int tarmac_random_select(int B, int N, int k, unsigned long long seed,
+                         unsigned long long offset, int64_t* idx_out,
+                         void* stream) {
+  if (!idx_out) return TARMAC_ERR_NULL;
+  if (B < 0 || N < 2) return TARMAC_ERR_SHAPE;
+  if (k < 1 || k > N - 1) return TARMAC_ERR_TOPK;
+  if (!aligned(idx_out, 8)) return TARMAC_ERR_ALIGN;
+  if (B == 0) return TARMAC_OK;
+  return launch_status(launch_random_select(B, N, k, seed, offset, idx_out,
+                                            (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -14,13 +14,15 @@ and forward signature ``forward(x, pos=None) -> (msg, info)``
                             (mappo.py:192-231, 374-382)
 ``zorder_k``                fused Z-order selection + attention over the
                             selected peers, 10-bit codes (mappo.py:265-292)
+``random_k``                k peers uniform at random (self excluded), then
+                            attention over them (mappo.py:233-263)
 
 The q, k, v chunks of the qkv output are passed to the kernels as strided
 views (no copies). Training works: the attention core's backward runs the
 gradient kernels (tarmac_b200.autograd), giving the gradients autograd forms
 through the reference's eager path (the peer selection carries none).
-Gradients of the top-k modes need k <= 8. The ``random_k``, ``entmax`` and
-``adaptive_topk`` study arms and the MAPPO actor/critic are outside this build.
+Gradients of the top-k modes need k <= 8. The ``entmax`` and ``adaptive_topk``
+study arms and the MAPPO actor/critic are outside this build.
 The weight-based diagnostics of ``collect_info`` (attention entropy) need the
 weight matrix, which the fused kernels never form; ``info`` carries
 ``effective_k`` where the reference reports it.
@@ -36,6 +38,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from tarmac_b200 import autograd as tgrad
+from tarmac_b200 import ops
 
 #: Slice of a simple_spread observation holding the agent's own position
 #: (mappo.py:24-28).
@@ -66,7 +69,8 @@ def _ortho_init(layer: nn.Linear, gain: float = float(np.sqrt(2.0))) -> None:
 class AttentionComm(nn.Module):
     """Inter-agent attention communication block: (B, N, D_in) -> (B, N, msg_dim)."""
 
-    _MODES = ("dense", "dense_sdpa", "topk", "topk_gather", "zorder_k")
+    _MODES = ("dense", "dense_sdpa", "topk", "topk_gather", "zorder_k",
+              "random_k")
 
     def __init__(self, cfg: MAPPOConfig, in_dim: int) -> None:
         super().__init__()
@@ -88,7 +92,7 @@ class AttentionComm(nn.Module):
         B, N, _ = x.shape
         mode = self.cfg.attn_mode
         if mode not in self._MODES:
-            if mode in ("random_k", "entmax", "adaptive_topk"):
+            if mode in ("entmax", "adaptive_topk"):
                 raise NotImplementedError(
                     f"attn_mode={mode!r} is outside the tarmac_b200 build")
             raise ValueError(f"unknown attn_mode {mode!r}")
@@ -103,6 +107,13 @@ class AttentionComm(nn.Module):
             info["effective_k"] = float(k_eff)
         elif mode in ("dense", "dense_sdpa"):
             msg = tgrad.dense_attention(q, k, v)
+        elif mode == "random_k":
+            # k peers uniform at random, self excluded (mappo.py:233-263);
+            # same gather-path aggregation as topk_gather
+            k_eff = self._k_eff(N)
+            idx = ops.random_select(B, N, k_eff, x.device)
+            msg = tgrad.prescore_attention(q, k, v, idx)
+            info["effective_k"] = float(k_eff)
         else:
             k_eff = self._k_eff(N)
             msg = tgrad.topk_attention(q, k, v, k_eff, "argmax")

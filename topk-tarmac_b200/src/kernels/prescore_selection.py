@@ -12,9 +12,14 @@ On the sm_100a kernels of ``tarmac_b200``:
 ``prescore_full(...)``             selector + attention; ``morton_window`` runs
                                    as one fused kernel (456-458)
 
-Outside this build (importable, raise NotImplementedError): the radius and
-grid kNN selectors (lines 293-300, 345-430) and the selector cost ledger
-``analytic_flops`` (lines 461-470).
+``select_radius_knn(pos, k)``      exact k nearest peers (lines 35-42)
+``select_grid_knn(pos, k)``        grid kNN with the reference's sizing and
+                                   capacity (lines 81-162); the cell order is
+                                   the stable one
+``grid_knn_recall(pos, k)``        membership recall of the grid selector
+
+Outside this build (importable, raises NotImplementedError): the selector
+cost ledger ``analytic_flops`` (lines 198-207).
 """
 
 from __future__ import annotations
@@ -47,18 +52,15 @@ def select_morton_window(pos: torch.Tensor, k: int,
     return ops.morton_select(pos, k, bits)
 
 
-def _not_built(name: str):
-    raise NotImplementedError(
-        f"{name} is outside the tarmac_b200 build (only the Morton window "
-        "selector is implemented on the GPU)")
-
-
 def select_radius_knn(pos: torch.Tensor, k: int) -> torch.Tensor:
-    _not_built("select_radius_knn")
+    """k spatially nearest peers per agent, int64 (B, N, k)
+    (prescore_selection.py:35-42): squared distances in fp32, self excluded,
+    peers by increasing (distance, index)."""
+    return ops.knn_select(pos, k)
 
 
 def grid_knn_shape(N: int, k: int) -> tuple[int, int]:
-    """Grid side G and per-cell capacity M (prescore_selection.py:345-359):
+    """Grid side G and per-cell capacity M (prescore_selection.py:81-97):
     cells sized for about max(2, k) agents, capacity mean + 3 sd + 2."""
     occ = max(2, k)
     G = max(1, int((N / occ) ** 0.5))
@@ -67,11 +69,28 @@ def grid_knn_shape(N: int, k: int) -> tuple[int, int]:
 
 
 def select_grid_knn(pos: torch.Tensor, k: int) -> torch.Tensor:
-    _not_built("select_grid_knn")
+    """k nearest peers among the 3x3 grid cells around each agent
+    (prescore_selection.py:103-162): the reference's grid and capacity, cells
+    sorted stably, the exact selector where the neighbourhood would hold N or
+    more candidates."""
+    return ops.grid_knn_select(pos, k)
 
 
 def grid_knn_recall(pos: torch.Tensor, k: int) -> float:
-    _not_built("grid_knn_recall")
+    """Fraction of retained peers that exact kNN would also retain
+    (prescore_selection.py:165-170)."""
+    got = select_grid_knn(pos, k)
+    ref = select_radius_knn(pos, k)
+    hit = (got.unsqueeze(-1) == ref.unsqueeze(-2)).any(-1)
+    return hit.float().mean().item()
+
+
+def analytic_flops(selector: str, B: int, N: int, d: int, kk: int) -> dict:
+    """The reference's selector cost ledger (src.analysis.selector_costs) is
+    outside this build."""
+    raise NotImplementedError(
+        "analytic_flops (src.analysis.selector_costs) is outside the "
+        "tarmac_b200 build")
 
 
 SELECTORS = {"radius_knn": select_radius_knn,
@@ -90,7 +109,3 @@ def prescore_full(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if selector == "morton_window":
         return ops.morton_prescore_attention(q, k, v, pos, kk, MORTON_BITS)
     return prescore_attention(q, k, v, SELECTORS[selector](pos, kk))
-
-
-def analytic_flops(selector: str, B: int, N: int, d: int, kk: int) -> dict:
-    _not_built("analytic_flops (the selector cost ledger)")

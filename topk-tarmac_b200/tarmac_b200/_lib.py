@@ -10,7 +10,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from ctypes import c_char_p, c_float, c_int, c_void_p
+from ctypes import c_char_p, c_float, c_int, c_uint64, c_void_p
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().with_name("libtarmac_b200.so")
@@ -61,6 +61,12 @@ SIGNATURES: dict[str, tuple] = {
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
         c_int, c_int, c_int, c_int, c_float, c_int, c_int, c_void_p,
         c_void_p]),
+    "tarmac_knn_select": (c_int, [
+        c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "tarmac_grid_knn_select": (c_int, [
+        c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
+    "tarmac_random_select": (c_int, [
+        c_int, c_int, c_int, c_uint64, c_uint64, c_void_p, c_void_p]),
     "tarmac_gather_attention_backward": (c_int, [
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
         c_int, c_int, c_int, c_int, c_int, c_int, c_float,

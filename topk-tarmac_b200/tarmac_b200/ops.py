@@ -285,3 +285,53 @@ def dense_attention_backward(q: torch.Tensor, k: torch.Tensor,
                   _DTYPES[q.dtype], _scale(d, scale), _ptr(dq), _ptr(dk),
                   _ptr(dv), _ptr(work), _stream(q.device))
     return dq, dk, dv
+
+
+# ---------------------------------------------------------------------------
+# positional and random selectors
+# ---------------------------------------------------------------------------
+
+SELECT_MAX_N = 8192
+SELECT_MAX_K = 32
+
+
+def knn_select(pos: torch.Tensor, k: int) -> torch.Tensor:
+    """Exact k nearest peers (self excluded), int64 [B, N, k], by increasing
+    (distance, index)."""
+    pos = _check_pos(pos)
+    B, N, _ = pos.shape
+    out = torch.empty((B, N, k), device=pos.device, dtype=torch.int64)
+    with torch.cuda.device(pos.device):
+        _lib.call("tarmac_knn_select", _ptr(pos), B, N, int(k), _ptr(out),
+                  _stream(pos.device))
+    return out
+
+
+def grid_knn_select(pos: torch.Tensor, k: int) -> torch.Tensor:
+    """k nearest among the 3 x 3 grid cells around each agent (the reference's
+    grid sizing and per-cell capacity), int64 [B, N, k]."""
+    pos = _check_pos(pos)
+    B, N, _ = pos.shape
+    out = torch.empty((B, N, k), device=pos.device, dtype=torch.int64)
+    with torch.cuda.device(pos.device):
+        _lib.call("tarmac_grid_knn_select", _ptr(pos), B, N, int(k),
+                  _ptr(out), _stream(pos.device))
+    return out
+
+
+def random_select(B: int, N: int, k: int, device,
+                  generator: torch.Generator | None = None) -> torch.Tensor:
+    """k distinct peers per agent, uniform over the k-subsets of the other
+    N - 1 agents, int64 [B, N, k]. The Philox key is drawn from ``generator``
+    (torch's default CPU generator when None), so torch.manual_seed fixes
+    the selection."""
+    device = torch.device(device)
+    if device.type != "cuda":
+        raise RuntimeError("tarmac_b200 kernels need a CUDA device")
+    seed, offset = (int(x) for x in torch.randint(
+        0, 2 ** 62, (2,), generator=generator))
+    out = torch.empty((B, N, k), device=device, dtype=torch.int64)
+    with torch.cuda.device(device):
+        _lib.call("tarmac_random_select", int(B), int(N), int(k), seed,
+                  offset, _ptr(out), _stream(device))
+    return out
