@@ -284,6 +284,59 @@ def _sweep_c5(ops, dev, stream) -> list:
     return rows
 
 
+def _comm_c1(ops, dev, stream) -> dict:
+    """BASELINE configs[0] shape through the whole comm module forward (qkv
+    Linear -> top-k core -> GELU -> proj), B=256, N=6, in_dim=64, msg_dim=16,
+    k=2, fp32: the fused one-kernel module against the layer-by-layer path
+    (cuBLAS Linear, the top-k kernel on strided q/k/v views, GELU, Linear).
+    Informational; warm (the inputs fit L2); 200 calls each."""
+    import torch
+    import torch.nn.functional as F
+    B, N, D, m, k = 256, 6, 64, 16, 2
+    g = torch.Generator().manual_seed(SEED)
+    x = torch.randn(B, N, D, generator=g).to(dev)
+    w_qkv = (torch.randn(3 * m, D, generator=g) / D ** 0.5).to(dev)
+    b_qkv = torch.zeros(3 * m).to(dev)
+    w_p = (torch.randn(m, m, generator=g) / m ** 0.5).to(dev)
+    b_p = torch.zeros(m).to(dev)
+
+    def fused(s):
+        ops.comm_forward(x, w_qkv, b_qkv, w_p, b_p, k)
+
+    def layered(s):
+        q, kk, v = F.linear(x, w_qkv, b_qkv).chunk(3, dim=-1)
+        F.linear(F.gelu(ops.topk_attention(q, kk, v, k)), w_p, b_p)
+
+    res = {"B": B, "N": N, "in_dim": D, "msg_dim": m, "k": k}
+    for name, fn in (("fused_us", fused), ("layered_us", layered)):
+        for s in range(5):
+            fn(s)
+        t = _time_loop(fn, 200, stream) / 200
+        res[name] = round(1e3 * t, 2)
+    res["fused_agent_rows_per_s"] = B * N / (res["fused_us"] * 1e-6)
+    # the same fused call replayed from a CUDA graph: device time without the
+    # per-call host work (argument checks, ctypes)
+    try:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            fused(0)
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for _ in range(20):
+                fused(0)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        t = _time_loop(lambda s: graph.replay(), 20, stream) / (20 * 20)
+        res["fused_graph_us"] = round(1e3 * t, 2)
+        del graph
+    except Exception as e:  # capture unsupported here: report why
+        res["fused_graph_us"] = None
+        res["graph_note"] = f"{type(e).__name__}: {e}"
+    return res
+
+
 def _fp32_peak(dev) -> float:
     """Measured fp32 (TF32 off) cuBLAS GEMM TFLOP/s: the FFMA roof the fp32
     top-k kernel is bound by (not a tensor-core figure)."""
@@ -449,6 +502,7 @@ def run_ours(args) -> int:
             sweep.append(row)
         del q_, k_, v_
     sweep_c5 = _sweep_c5(ops, dev, stream) if rank == 0 and not args.no_sweep else []
+    comm_c1 = _comm_c1(ops, dev, stream) if rank == 0 and not args.no_sweep else {}
 
     fp32_tf = _fp32_peak(dev) if rank == 0 else None
     if multi:
@@ -496,6 +550,7 @@ def run_ours(args) -> int:
         "clocks": clk.summary(),
         "sweep_c2_us": sweep,
         "sweep_c5_bf16": sweep_c5,
+        "comm_module_c1": comm_c1,
     }
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(args.cpu_episodes, args.cpu_seconds)

@@ -191,6 +191,23 @@ int tarmac_random_select(int B, int N, int k, unsigned long long seed,
                          unsigned long long offset, int64_t *idx_out,
                          void *stream);
 
+/* ---- the whole communication module (inference) --------------------------- */
+/* AttentionComm.forward for the dense and top-k modes in one kernel
+ * (src/agents/mappo.py:332-353, 361-373, 419-420):
+ *   q, k, v = split(x W_qkv^T + b_qkv)      (nn.Linear layout: W [out, in])
+ *   msg = dense attention (topk == 0) or top-k attention (1 <= topk <= 8,
+ *         lowest index on a tie), diagonal excluded, scale 1/sqrt(msg_dim)
+ *   out = gelu(msg) W_proj^T + b_proj          (exact erf GELU)
+ * x: fp32 [B, N, in_dim] contiguous; weights fp32 contiguous; out: fp32
+ * [B, N, msg_dim]. Q, K, V never leave the SM. 2 <= N, 1 <= in_dim <= 256,
+ * 1 <= msg_dim <= 64, topk <= N - 1; the episode's Q, K and V must fit
+ * shared memory (N * msg_dim up to about 16 K values; TARMAC_ERR_N_TOO_LARGE
+ * otherwise). */
+int tarmac_comm_forward(const float *x, const float *w_qkv, const float *b_qkv,
+                        const float *w_proj, const float *b_proj, int B, int N,
+                        int in_dim, int msg_dim, int topk, float *out,
+                        void *stream);
+
 /* ---- gradients (training) ------------------------------------------------ */
 /* The reference trains through its eager path and autograd
  * (src/agents/mappo.py:192-231 topk_gather, 265-292 zorder_k, 361-373 dense);

@@ -14,7 +14,7 @@ and ``--impl reference`` legs may import it. The product path
 """
 
 from .tarmac_oracle import (  # noqa: F401
-    ambiguous_rows, dense_attention, dense_attention_grad,
+    ambiguous_rows, comm_forward, dense_attention, dense_attention_grad,
     gather_attention_grad, grid_knn, grid_knn_shape, knn_ambiguous,
     knn_exact, morton_code, morton_window, prescore_attention, scores_f32,
     scores_f64, select_mask, topk_attention, topk_indices)

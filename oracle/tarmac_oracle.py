@@ -376,6 +376,41 @@ def grid_knn(pos: np.ndarray, k: int) -> np.ndarray:
     return out
 
 
+# ---------------------------------------------------------------------------
+# the communication module forward
+# ---------------------------------------------------------------------------
+
+def _gelu_erf(x: np.ndarray) -> np.ndarray:
+    from scipy.special import erf
+    return 0.5 * x * (1.0 + erf(x / np.sqrt(2.0)))
+
+
+def comm_forward(x, w_qkv, b_qkv, w_proj, b_proj, topk: int):
+    """AttentionComm.forward, float64 (src/agents/mappo.py:332-353, 361-373,
+    419-420): q, k, v = split(x W_qkv^T + b_qkv); dense softmax (topk == 0)
+    or the top-k gathered softmax with the lowest index on a tie; then
+    gelu(msg) W_proj^T + b_proj with the exact GELU. Returns (out, q, k) so
+    callers can classify near-tie rows on the same q, k."""
+    x = np.asarray(x, dtype=np.float64)
+    qkv = x @ np.asarray(w_qkv, np.float64).T + np.asarray(b_qkv, np.float64)
+    m = qkv.shape[-1] // 3
+    q, k, v = qkv[..., :m], qkv[..., m:2 * m], qkv[..., 2 * m:]
+    B, N, _ = q.shape
+    s = np.einsum("bid,bjd->bij", q, k) / np.sqrt(m)
+    s[:, np.arange(N), np.arange(N)] = -np.inf
+    if topk:
+        keep = np.zeros_like(s, dtype=bool)
+        idx = np.argsort(-s, axis=-1, kind="stable")[..., :topk]
+        np.put_along_axis(keep, idx, True, axis=-1)
+        s = np.where(keep, s, -np.inf)
+    w = np.exp(s - s.max(-1, keepdims=True))
+    w /= w.sum(-1, keepdims=True)
+    msg = np.einsum("bij,bjd->bid", w, v)
+    out = _gelu_erf(msg) @ np.asarray(w_proj, np.float64).T + \
+        np.asarray(b_proj, np.float64)
+    return out, q, k
+
+
 _SPREAD = ((8, 0x00FF00FF), (4, 0x0F0F0F0F), (2, 0x33333333), (1, 0x55555555))
 
 

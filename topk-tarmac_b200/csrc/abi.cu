@@ -6,6 +6,7 @@
 #include <math.h>
 
 #include "backward.cuh"
+#include "comm.cuh"
 #include "common.cuh"
 #include "topk_chunk.cuh"
 
@@ -383,6 +384,32 @@ int tarmac_random_select(int B, int N, int k, unsigned long long seed,
   if (B == 0) return TARMAC_OK;
   return launch_status(launch_random_select(B, N, k, seed, offset, idx_out,
                                             (cudaStream_t)stream));
+}
+
+int tarmac_comm_forward(const float* x, const float* w_qkv, const float* b_qkv,
+                        const float* w_proj, const float* b_proj, int B, int N,
+                        int in_dim, int msg_dim, int topk, float* out,
+                        void* stream) {
+  if (!x || !w_qkv || !b_qkv || !w_proj || !b_proj || !out)
+    return TARMAC_ERR_NULL;
+  if (B < 0 || N < 2 || in_dim < 1 || in_dim > 256 || msg_dim < 1 ||
+      msg_dim > 64)
+    return TARMAC_ERR_SHAPE;
+  if (topk < 0 || topk > N - 1 || topk > REGISTER_MAX_K) return TARMAC_ERR_TOPK;
+  const void* ptrs[6] = {x, w_qkv, b_qkv, w_proj, b_proj, out};
+  for (const void* ptr : ptrs)
+    if (!aligned(ptr, 4)) return TARMAC_ERR_ALIGN;
+  if (comm_smem_bytes(N, in_dim, msg_dim, comm_padded_m(msg_dim)) >
+      (size_t)227 * 1024)
+    return TARMAC_ERR_N_TOO_LARGE;
+  if (B == 0) return TARMAC_OK;
+  CommParams p;
+  p.x = x; p.wqkv = w_qkv; p.bqkv = b_qkv; p.wproj = w_proj; p.bproj = b_proj;
+  p.out = out;
+  p.B = B; p.N = N; p.in_dim = in_dim; p.m = msg_dim;
+  p.topk = topk;
+  p.scale = 1.0f / sqrtf((float)msg_dim);
+  return launch_status(launch_comm_forward(p, (cudaStream_t)stream));
 }
 
 }  // extern "C"

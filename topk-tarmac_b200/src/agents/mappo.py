@@ -17,8 +17,10 @@ and forward signature ``forward(x, pos=None) -> (msg, info)``
 ``random_k``                k peers uniform at random (self excluded), then
                             attention over them (mappo.py:233-263)
 
-The q, k, v chunks of the qkv output are passed to the kernels as strided
-views (no copies). Training works: the attention core's backward runs the
+In inference (no gradient needed), fp32, the dense and top-k modes run the
+whole module (qkv projection, attention core, GELU, output projection) as one
+kernel in which Q, K and V never leave the SM. Otherwise the q, k, v chunks
+of the qkv output are passed to the kernels as strided views (no copies). Training works: the attention core's backward runs the
 gradient kernels (tarmac_b200.autograd), giving the gradients autograd forms
 through the reference's eager path (the peer selection carries none).
 Gradients of the top-k modes need k <= 8. The ``entmax`` and ``adaptive_topk``
@@ -87,6 +89,22 @@ class AttentionComm(nn.Module):
     def _k_eff(self, N: int) -> int:
         return min(max(self.cfg.topk, 1), N - 1)
 
+    #: largest episode the fused module kernel takes (its K and V rows sit in
+    #: shared memory)
+    FUSED_MAX_N = 1024
+
+    def _fused_ok(self, x: torch.Tensor, mode: str, N: int) -> bool:
+        if torch.is_grad_enabled() and (
+                x.requires_grad or any(p.requires_grad for p in self.parameters())):
+            return False
+        if mode not in ("dense", "dense_sdpa", "topk", "topk_gather"):
+            return False
+        if mode in ("topk", "topk_gather") and self._k_eff(N) > 8:
+            return False
+        m, D = self.cfg.msg_dim, x.shape[-1]
+        return (x.is_cuda and x.dtype == torch.float32 and 2 <= N and
+                m <= 64 and D <= 256 and N * m <= 16384 and N <= self.FUSED_MAX_N)
+
     def forward(self, x: torch.Tensor,
                 pos: torch.Tensor | None = None) -> tuple[torch.Tensor, dict]:
         B, N, _ = x.shape
@@ -96,8 +114,16 @@ class AttentionComm(nn.Module):
                 raise NotImplementedError(
                     f"attn_mode={mode!r} is outside the tarmac_b200 build")
             raise ValueError(f"unknown attn_mode {mode!r}")
-        q, k, v = self.qkv(x).chunk(3, dim=-1)
         info: dict = {}
+        if self._fused_ok(x, mode, N):
+            # inference: the whole module (qkv, core, gelu, proj) is one kernel
+            k_eff = 0 if mode in ("dense", "dense_sdpa") else self._k_eff(N)
+            if k_eff:
+                info["effective_k"] = float(k_eff)
+            return ops.comm_forward(x, self.qkv.weight, self.qkv.bias,
+                                    self.proj.weight, self.proj.bias,
+                                    k_eff), info
+        q, k, v = self.qkv(x).chunk(3, dim=-1)
         if mode == "zorder_k":
             if pos is None:
                 raise ValueError("attn_mode='zorder_k' needs agent positions")

@@ -67,6 +67,9 @@ SIGNATURES: dict[str, tuple] = {
         c_void_p, c_int, c_int, c_int, c_void_p, c_void_p]),
     "tarmac_random_select": (c_int, [
         c_int, c_int, c_int, c_uint64, c_uint64, c_void_p, c_void_p]),
+    "tarmac_comm_forward": (c_int, [
+        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+        c_int, c_int, c_int, c_int, c_int, c_void_p, c_void_p]),
     "tarmac_gather_attention_backward": (c_int, [
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
         c_int, c_int, c_int, c_int, c_int, c_int, c_float,

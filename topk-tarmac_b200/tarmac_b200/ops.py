@@ -335,3 +335,33 @@ def random_select(B: int, N: int, k: int, device,
         _lib.call("tarmac_random_select", int(B), int(N), int(k), seed,
                   offset, _ptr(out), _stream(device))
     return out
+
+
+# ---------------------------------------------------------------------------
+# the whole communication module (inference)
+# ---------------------------------------------------------------------------
+
+def comm_forward(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor,
+                 w_proj: torch.Tensor, b_proj: torch.Tensor,
+                 topk: int) -> torch.Tensor:
+    """gelu(attention(split(x W_qkv^T + b_qkv))) W_proj^T + b_proj in one
+    kernel: dense attention for ``topk == 0``, else top-k (k <= 8, lowest
+    index on a tie). fp32, inference only (no autograd)."""
+    if not x.is_cuda:
+        raise RuntimeError("tarmac_b200 kernels need CUDA tensors")
+    if x.dim() != 3:
+        raise ValueError(f"x must be [B, N, in_dim]; got {tuple(x.shape)}")
+    ts = [t.contiguous().float() for t in (x, w_qkv, b_qkv, w_proj, b_proj)]
+    x, w_qkv, b_qkv, w_proj, b_proj = ts
+    B, N, D = x.shape
+    m = w_proj.shape[0]
+    if w_qkv.shape != (3 * m, D) or b_qkv.shape != (3 * m,) or \
+            w_proj.shape != (m, m) or b_proj.shape != (m,):
+        raise ValueError("weights must be qkv [3m, in_dim], [3m] and proj "
+                         "[m, m], [m]")
+    out = torch.empty((B, N, m), device=x.device, dtype=torch.float32)
+    with torch.cuda.device(x.device):
+        _lib.call("tarmac_comm_forward", _ptr(x), _ptr(w_qkv), _ptr(b_qkv),
+                  _ptr(w_proj), _ptr(b_proj), B, N, D, m, int(topk),
+                  _ptr(out), _stream(x.device))
+    return out
