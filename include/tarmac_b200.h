@@ -56,6 +56,8 @@ extern "C" {
 #define TARMAC_ERR_MODE 7       /* unknown selection mode / unsupported combo */
 #define TARMAC_ERR_LAUNCH 8     /* the CUDA launch itself failed              */
 #define TARMAC_ERR_BITS 9       /* Morton bits outside [1, 16]                */
+#define TARMAC_ERR_SCRATCH 10   /* problem larger than the library's fixed
+                                   scratch (no-allocation entry point)      */
 
 /* ---- element types ------------------------------------------------------- */
 #define TARMAC_F32 0
@@ -251,6 +253,30 @@ int tarmac_dense_attention_backward(const void *q, const void *k,
                                     int B, int N, int d, int dtype, float scale,
                                     float *dq, float *dk, float *dv,
                                     float *work, void *stream);
+
+/* Dense-attention gradients without a caller workspace: the same result as
+ * tarmac_dense_attention_backward, with the row statistics held in a fixed
+ * 4 MiB device array inside the library instead of the `work` buffer. It has
+ * no counterpart in the reference. It is for callers that cannot allocate
+ * device memory: code run under a memory manager that owns every device
+ * allocation and hands the library only its inputs and outputs, or a loop
+ * that must not allocate once running, because a device allocation can
+ * synchronise the device and take unbounded time. This call allocates
+ * nothing (no cudaMalloc, no allocating library routine); the array is part
+ * of the library image, so every GPU that loads the library holds it until
+ * the process exits.
+ * Limit: B * N <= 524288 query rows (TARMAC_ERR_SCRATCH beyond).
+ * The first call on a device looks up the array's device address on that
+ * device (the device current at the call, which must be the device of the
+ * pointers); make that first call before any stream capture. Every call
+ * shares the one array: calls that overlap on the GPU (other streams, other
+ * threads) race on it, so serialise them. No scratch contents need to start
+ * at zero (each call writes the statistics before reading them).
+ * Arguments as tarmac_dense_attention_backward, without `work`. */
+int tarmac_dense_attention_backward_noalloc(
+    const void *q, const void *k, const void *v, const void *out,
+    const void *dout, const int64_t *strides, int B, int N, int d, int dtype,
+    float scale, float *dq, float *dk, float *dv, void *stream);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

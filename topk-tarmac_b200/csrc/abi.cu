@@ -56,6 +56,8 @@ cudaError_t launch_grid_knn_select(const float* pos, int B, int N, int k,
 cudaError_t launch_random_select(int B, int N, int k, unsigned long long seed,
                                  unsigned long long offset, int64_t* out,
                                  cudaStream_t s);
+size_t noalloc_scratch_floats();
+cudaError_t noalloc_scratch(float** ptr);
 cudaError_t launch_morton_prescore(const AttnParams& p, int dtype,
                                    const float* pos, int bits,
                                    int64_t* idx_out, cudaStream_t s);
@@ -191,6 +193,8 @@ const char* tarmac_strerror(int status) {
     case TARMAC_ERR_MODE: return "unknown selection mode or unsupported combination";
     case TARMAC_ERR_LAUNCH: return "CUDA kernel launch failed";
     case TARMAC_ERR_BITS: return "Morton bits must lie in [1, 16]";
+    case TARMAC_ERR_SCRATCH:
+      return "problem larger than the library's fixed scratch (B * N <= 524288)";
     default: return "unknown status";
   }
 }
@@ -410,6 +414,27 @@ int tarmac_comm_forward(const float* x, const float* w_qkv, const float* b_qkv,
   p.topk = topk;
   p.scale = 1.0f / sqrtf((float)msg_dim);
   return launch_status(launch_comm_forward(p, (cudaStream_t)stream));
+}
+
+// The dense-attention gradient with the row statistics in the library's
+// fixed device scratch (noalloc.cu) instead of a caller workspace; allocates
+// nothing.
+int tarmac_dense_attention_backward_noalloc(
+    const void* q, const void* k, const void* v, const void* out,
+    const void* dout, const int64_t* strides, int B, int N, int d, int dtype,
+    float scale, float* dq, float* dk, float* dv, void* stream) {
+  BwdParams p;
+  int st = fill_bwd(p, q, k, v, out, dout, strides, 10, B, N, d, dtype, scale,
+                    dq, dk, dv);
+  if (st != TARMAC_OK) return st;
+  if ((size_t)2 * (size_t)B * (size_t)N > noalloc_scratch_floats())
+    return TARMAC_ERR_SCRATCH;
+  if (B == 0) return TARMAC_OK;
+  float* scratch = nullptr;
+  if (noalloc_scratch(&scratch) != cudaSuccess) return TARMAC_ERR_LAUNCH;
+  p.work = scratch;
+  return launch_status(
+      launch_dense_bwd(p, dtype == TARMAC_BF16, (cudaStream_t)stream));
 }
 
 }  // extern "C"

@@ -27,6 +27,7 @@ ERR_ALIGN = 6
 ERR_MODE = 7
 ERR_LAUNCH = 8
 ERR_BITS = 9
+ERR_SCRATCH = 10
 
 F32 = 0
 BF16 = 1
@@ -78,6 +79,10 @@ SIGNATURES: dict[str, tuple] = {
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
         c_int, c_int, c_int, c_int, c_float,
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "tarmac_dense_attention_backward_noalloc": (c_int, [
+        c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+        c_int, c_int, c_int, c_int, c_float,
+        c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _LOCK = threading.Lock()
