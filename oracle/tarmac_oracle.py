@@ -247,10 +247,12 @@ def gather_attention_grad(q, k, v, idx, g, scale: float | None = None):
     return dq, dk, dv
 
 
-def dense_attention_grad(q, k, v, g, scale: float | None = None):
+def dense_attention_grad(q, k, v, g, scale: float | None = None, out=None):
     """Gradients (dq, dk, dv) of dense masked-diagonal attention, float64:
     the chain rule through the eager path's matmul, masked softmax and matmul
-    (src/agents/mappo.py:361-373)."""
+    (src/agents/mappo.py:361-373). ``out`` (optional) is the forward output
+    that D_i = g_i . out_i is taken from, as a kernel given a stored (e.g.
+    bf16-rounded) output forms it; by default the exact output."""
     B, N, d = q.shape
     sc = 1.0 / np.sqrt(d) if scale is None else float(scale)
     q64, k64, v64, g64 = (np.asarray(t, dtype=np.float64) for t in (q, k, v, g))
@@ -258,9 +260,10 @@ def dense_attention_grad(q, k, v, g, scale: float | None = None):
     s[:, np.arange(N), np.arange(N)] = -np.inf
     p = np.exp(s - s.max(-1, keepdims=True))
     p /= p.sum(-1, keepdims=True)
-    out = np.einsum("bij,bjd->bid", p, v64)
+    o64 = (np.einsum("bij,bjd->bid", p, v64) if out is None
+           else np.asarray(out, dtype=np.float64))
     dp = np.einsum("bid,bjd->bij", g64, v64)
-    dsc = p * (dp - (g64 * out).sum(-1)[..., None])
+    dsc = p * (dp - (g64 * o64).sum(-1)[..., None])
     dq = sc * np.einsum("bij,bjd->bid", dsc, k64)
     dk = sc * np.einsum("bij,bid->bjd", dsc, q64)
     dv = np.einsum("bij,bid->bjd", p, g64)

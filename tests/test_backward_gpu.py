@@ -44,6 +44,22 @@ def test_dense_backward(tb, N, d):
         close(a, b)
 
 
+@pytest.mark.parametrize("N,d", [(6, 16), (128, 16), (300, 32), (512, 64)])
+def test_dense_backward_bf16(tb, N, d):
+    """bf16 inputs (fp32 arithmetic on the widened values); D from the
+    bf16 forward output the kernel is given."""
+    ops, _ = tb
+    q, k, v = qkv(3, N, d, seed=N * 5 + d, dtype=torch.bfloat16)
+    g = torch.randn(3, N, d, generator=torch.Generator().manual_seed(N))
+    g = g.to(torch.bfloat16).cuda()
+    out = ops.dense_attention(q, k, v)
+    dq, dk, dv = ops.dense_attention_backward(q, k, v, out, g)
+    want = oracle.dense_attention_grad(host(q), host(k), host(v), host(g),
+                                       out=host(out))
+    for a, b in zip((dq, dk, dv), want):
+        close(a, b)
+
+
 @pytest.mark.parametrize("N,d,kk,itype,dup", [
     (8, 16, 2, torch.int64, False), (64, 16, 4, torch.int32, False),
     (300, 32, 3, torch.int64, True), (512, 16, 8, torch.int32, False),
