@@ -413,6 +413,7 @@ int tarmac_comm_forward(const float* x, const float* w_qkv, const float* b_qkv,
   p.B = B; p.N = N; p.in_dim = in_dim; p.m = msg_dim;
   p.topk = topk;
   p.scale = 1.0f / sqrtf((float)msg_dim);
+  p.w_smem = 0;
   return launch_status(launch_comm_forward(p, (cudaStream_t)stream));
 }
 

@@ -8,11 +8,12 @@
 // topk / topk_gather function); out = gelu(msg) W_proj^T + b_proj with the
 // exact (erf) GELU of torch.nn.functional.gelu.
 //
-// One block owns one episode. The output projection and the episode's Q, K
-// and V rows (msg_dim wide) sit in shared memory, so Q, K and V never reach HBM:
-// the kernel reads x once and writes the module output once. Phase 1: every
-// thread projects its agents' x rows (staged through shared memory 32 rows
-// at a time, coalesced) into q (kept in shared memory too), k and v. Phase 2:
+// One block owns one episode. The projections and the episode's Q, K and V
+// rows (msg_dim wide) sit in shared memory, so Q, K and V never reach HBM:
+// the kernel reads x once and writes the module output once. Phase 1: the
+// block projects the episode's x rows (staged through shared memory 32 rows
+// at a time, coalesced) into q, k and v, one (row, output) pair per thread
+// at a time. Phase 2:
 // every thread owns query agents: scores against all keys (fp32 FMA), a
 // sorted k-best buffer (top-k) or a base-2 online softmax (dense), the V
 // aggregate, GELU and the output projection. Sized for the reference's
@@ -32,48 +33,58 @@ __device__ __forceinline__ float gelu_erf(float x) {
 }
 
 // Dynamic shared memory layout (floats): W_proj [m][m], b_proj [m], Q/K/V
-// [N][MP] each (columns m..MP-1 zero), x tile [32][in_dim + 1] (the pad puts
-// the 32 rows a warp reads on distinct banks). W_qkv is read from global
-// memory: the lanes of a warp read the same element at the same time, a
-// broadcast served by L1.
+// [N][MP] each (columns m..MP-1 zero), x tile [32][in_dim + 1], and, when
+// p.w_smem, W_qkv [3m][in_dim + 1] (both pads put a warp's 32 reads on
+// distinct banks). Without p.w_smem W_qkv is read from global memory
+// through L1.
 template <int MP, int KM>
 __global__ void __launch_bounds__(COMM_THREADS) comm_forward_kernel(CommParams p) {
   extern __shared__ __align__(16) float comm_sm[];
   const int N = p.N, D = p.in_dim, m = p.m;
+  const int DS = D + 1;
   float* spw = comm_sm;
   float* spb = spw + m * m;
   float* sq = spb + m;
   float* sk = sq + (size_t)N * MP;
   float* sv = sk + (size_t)N * MP;
   float* sx = sv + (size_t)N * MP;
+  float* sw = sx + (size_t)COMM_XTILE * DS;
   const int b = blockIdx.x;
   const float* X = p.x + (int64_t)b * N * D;
 
   for (int e = threadIdx.x; e < m * m; e += blockDim.x) spw[e] = p.wproj[e];
   for (int e = threadIdx.x; e < m; e += blockDim.x) spb[e] = p.bproj[e];
   for (int e = threadIdx.x; e < 3 * N * MP; e += blockDim.x) sq[e] = 0.f;
-  const int DS = D + 1;
+  if (p.w_smem)
+    for (int e = threadIdx.x; e < 3 * m * D; e += blockDim.x)
+      sw[(e / D) * DS + e % D] = p.wqkv[e];
 
   // ---- phase 1: q, k, v rows of every agent --------------------------------
+  // Threads take (row, output) pairs of the staged tile, consecutive threads
+  // consecutive outputs of one row: the x row is a broadcast read, the
+  // weight rows distinct banks.
+  const int M3 = 3 * m;
   for (int r0 = 0; r0 < N; r0 += COMM_XTILE) {
     const int nr = min(COMM_XTILE, N - r0);
     __syncthreads();
     for (int e = threadIdx.x; e < nr * D; e += blockDim.x)
       sx[(e / D) * DS + e % D] = X[(int64_t)r0 * D + e];
     __syncthreads();
-    // thread t: row t % 32 of the tile, output columns (t / 32) + 4c
-    const int rr = threadIdx.x & 31;
-    if (rr < nr) {
+    for (int pr = threadIdx.x; pr < nr * M3; pr += blockDim.x) {
+      const int rr = pr / M3, o = pr - rr * M3;
       const float* xr = sx + rr * DS;
-      for (int o = threadIdx.x >> 5; o < 3 * m; o += COMM_THREADS / 32) {
+      float acc = 0.f;
+      if (p.w_smem) {
+        const float* wr = sw + o * DS;
+        for (int c = 0; c < D; ++c) acc = fmaf(xr[c], wr[c], acc);
+      } else {
         const float* wr = p.wqkv + (int64_t)o * D;
-        float acc = 0.f;
         for (int c = 0; c < D; ++c) acc = fmaf(xr[c], __ldg(wr + c), acc);
-        acc += __ldg(p.bqkv + o);
-        const int part = o / m, col = o - part * m;
-        float* dst = part == 0 ? sq : (part == 1 ? sk : sv);
-        dst[(r0 + rr) * MP + col] = acc;
       }
+      acc += __ldg(p.bqkv + o);
+      const int part = o / m, col = o - part * m;
+      float* dst = part == 0 ? sq : (part == 1 ? sk : sv);
+      dst[(r0 + rr) * MP + col] = acc;
     }
   }
   __syncthreads();
@@ -162,9 +173,15 @@ size_t comm_smem_bytes(int N, int in_dim, int m, int MP) {
                           (size_t)COMM_XTILE * (in_dim + 1));
 }
 
+// W_qkv joins the block's shared memory when the total stays within this
+static constexpr size_t COMM_SMEM_WITH_W = 160 * 1024;
+
 template <int MP, int KM>
-static cudaError_t launch_comm_t(const CommParams& p, cudaStream_t s) {
-  const size_t sm = comm_smem_bytes(p.N, p.in_dim, p.m, MP);
+static cudaError_t launch_comm_t(CommParams p, cudaStream_t s) {
+  size_t sm = comm_smem_bytes(p.N, p.in_dim, p.m, MP);
+  const size_t wb = sizeof(float) * (size_t)3 * p.m * (p.in_dim + 1);
+  p.w_smem = sm + wb <= COMM_SMEM_WITH_W;
+  if (p.w_smem) sm += wb;
   cudaError_t e = cudaFuncSetAttribute(comm_forward_kernel<MP, KM>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sm);

@@ -16,6 +16,7 @@ struct CommParams {
   int B, N, in_dim, m;
   int topk;              // 0: dense
   float scale;           // 1/sqrt(m)
+  int w_smem;            // W_qkv staged in shared memory (set by the launcher)
 };
 
 cudaError_t launch_comm_forward(const CommParams& p, cudaStream_t s);
