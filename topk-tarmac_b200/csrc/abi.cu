@@ -22,15 +22,21 @@ cudaError_t launch_topk_chunk_bf16_high(const AttnParams& p, cudaStream_t s);
 
 bool topk_tc_supported(const AttnParams& p);
 cudaError_t launch_topk_tc(const AttnParams& p, bool tie_high, cudaStream_t s);
+bool topk_tc_f32_supported(const AttnParams& p);
+cudaError_t launch_topk_tc_f32(const AttnParams& p, bool tie_high,
+                               cudaStream_t s);
 
-// k <= 8 with the lowest- or highest-index tie rule: bf16 episodes of 128 to
-// 512 agents form their scores on the tensor cores; otherwise the chunked
-// FFMA kernel when the episode's keys fit its shared memory, else the
-// streaming kernel.
+// k <= 8 with the lowest- or highest-index tie rule: episodes of 128 agents
+// or more form their scores on the tensor cores (bf16 directly; fp32 as
+// three exact bf16 planes, d a multiple of 8 up to 16, 16-byte rows);
+// otherwise the chunked FFMA kernel when the episode's keys fit its shared
+// memory, else the streaming kernel.
 static cudaError_t launch_topk_small_k(const AttnParams& p, int dtype,
                                        bool tie_high, cudaStream_t s) {
   if (dtype == TARMAC_BF16 && topk_tc_supported(p))
     return launch_topk_tc(p, tie_high, s);
+  if (dtype == TARMAC_F32 && topk_tc_f32_supported(p))
+    return launch_topk_tc_f32(p, tie_high, s);
   if (chunk_fits(p.N, p.d, p.topk)) {
     if (dtype == TARMAC_BF16)
       return tie_high ? launch_topk_chunk_bf16_high(p, s)

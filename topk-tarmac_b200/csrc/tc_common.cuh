@@ -311,31 +311,34 @@ __device__ __forceinline__ float ex2_approx(float x) {
 
 // Row-cooperative gather-aggregate-store over the 32 query rows of a warp.
 // Lane t owns row row0 + t: its KC candidate indices idx (used for m < kk),
-// their normalised weights w and a NaN-row flag. DP/8 lanes share a row and
-// each moves 16 bytes (8 bf16) of every gathered V row and of the output
-// row, so one warp instruction touches 32/(DP/8) whole rows rather than 32
-// scattered pieces. The owners first prefetch their V rows into L2; the
-// loads then go out in batches of up to 16 per lane before any is used.
-// Requires d % 8 == 0 and 16-byte aligned V and O rows. Every lane of the
-// warp must call it (the row data moves by shuffles).
-template <int DP, int KC>
+// their normalised weights w and a NaN-row flag. DP/EPV lanes share a row
+// (EPV = elements per 16 bytes: 8 bf16 or 4 fp32) and each moves 16 bytes of
+// every gathered V row and of the output row, so one warp instruction touches
+// 32/(DP/EPV) whole rows rather than 32 scattered pieces. The owners first
+// prefetch their V rows into L2; the loads then go out in batches of up to 16
+// per lane before any is used. Requires d % EPV == 0 and 16-byte aligned V
+// and O rows. Every lane of the warp must call it (the row data moves by
+// shuffles).
+template <typename T, int DP, int KC>
 __device__ __forceinline__ void coop_gather_store(
-    const __nv_bfloat16* V, int64_t vn, __nv_bfloat16* O, int64_t on,
-    int row0, int N, int d, int kk, const int (&idx)[KC],
-    const float (&w)[KC], bool nan_row) {
-  constexpr int LPR = DP / 8;  // lanes per row
+    const T* V, int64_t vn, T* O, int64_t on, int row0, int N, int d, int kk,
+    const int (&idx)[KC], const float (&w)[KC], bool nan_row) {
+  constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte piece
+  constexpr int LPR = DP / EPV;             // lanes per row
   constexpr int RPI = 32 / LPR;
   constexpr int GI = KC >= 16 ? 1 : (16 / KC < LPR ? 16 / KC : LPR);
+  constexpr int LINE = 128 / (int)sizeof(T);  // elements per 128-byte line
+  static_assert(LPR >= 1 && LPR <= 32, "row width");
   const int lane = threadIdx.x & 31;
   const int sub = lane % LPR, rsub = lane / LPR;
-  const int c0 = sub * 8;
+  const int c0 = sub * EPV;
   if (row0 + lane < N) {
 #pragma unroll
     for (int m = 0; m < KC; ++m)
       if (m < kk && idx[m] >= 0) {
-        const __nv_bfloat16* vr = V + (int64_t)idx[m] * vn;
+        const T* vr = V + (int64_t)idx[m] * vn;
 #pragma unroll
-        for (int c = 0; c < DP; c += 64)
+        for (int c = 0; c < DP; c += LINE)
           if (c < d) asm volatile("prefetch.global.L2 [%0];" ::"l"(vr + c));
       }
   }
@@ -363,38 +366,140 @@ __device__ __forceinline__ void coop_gather_store(
       const int src = (i0 + g) * RPI + rsub;
       const int r = row0 + src;
       const bool bad = __shfl_sync(0xffffffffu, (int)nan_row, src) != 0;
-      float acc[8];
+      float acc[EPV];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) acc[u] = 0.f;
+      for (int u = 0; u < EPV; ++u) acc[u] = 0.f;
 #pragma unroll
       for (int m = 0; m < KC; ++m) {
         const uint32_t h[4] = {raw[g][m].x, raw[g][m].y, raw[g][m].z,
                                raw[g][m].w};
+        float f[EPV];
+        if constexpr (sizeof(T) == 2) {
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float2 f = __bfloat1622float2(
-              *reinterpret_cast<const __nv_bfloat162*>(&h[u]));
-          const float a0 = fmaf(wm[g][m], f.x, acc[2 * u]);
-          const float a1 = fmaf(wm[g][m], f.y, acc[2 * u + 1]);
-          acc[2 * u] = use[g][m] ? a0 : acc[2 * u];
-          acc[2 * u + 1] = use[g][m] ? a1 : acc[2 * u + 1];
+          for (int u = 0; u < 4; ++u) {
+            const float2 t = __bfloat1622float2(
+                *reinterpret_cast<const __nv_bfloat162*>(&h[u]));
+            f[2 * u] = t.x;
+            f[2 * u + 1] = t.y;
+          }
+        } else {
+#pragma unroll
+          for (int u = 0; u < 4; ++u) f[u] = __uint_as_float(h[u]);
+        }
+#pragma unroll
+        for (int u = 0; u < EPV; ++u) {
+          const float a = fmaf(wm[g][m], f[u], acc[u]);
+          acc[u] = use[g][m] ? a : acc[u];
         }
       }
       if (r < N && c0 < d) {
         uint4 out;
-        if (bad) {
-          out = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u);
+        if constexpr (sizeof(T) == 2) {
+          if (bad) {
+            out = make_uint4(0x7fc07fc0u, 0x7fc07fc0u, 0x7fc07fc0u,
+                             0x7fc07fc0u);
+          } else {
+            out.x = pack_bf16x2(acc[0], acc[1]);
+            out.y = pack_bf16x2(acc[2], acc[3]);
+            out.z = pack_bf16x2(acc[4], acc[5]);
+            out.w = pack_bf16x2(acc[6], acc[7]);
+          }
         } else {
-          out.x = pack_bf16x2(acc[0], acc[1]);
-          out.y = pack_bf16x2(acc[2], acc[3]);
-          out.z = pack_bf16x2(acc[4], acc[5]);
-          out.w = pack_bf16x2(acc[6], acc[7]);
+          if (bad) {
+            out = make_uint4(0x7fc00000u, 0x7fc00000u, 0x7fc00000u,
+                             0x7fc00000u);
+          } else {
+            out = make_uint4(__float_as_uint(acc[0]), __float_as_uint(acc[1]),
+                             __float_as_uint(acc[2]), __float_as_uint(acc[3]));
+          }
         }
         *reinterpret_cast<uint4*>(O + (int64_t)r * on + c0) = out;
       }
     }
   }
 }
+
+// ---------------------------------------------------------------------------
+// fp32 operands on the bf16 tensor cores
+// ---------------------------------------------------------------------------
+// An fp32 value x is the exact sum of three bf16 values, each rounded to
+// nearest: hi = bf16(x) keeps the leading 8 significant bits; x - hi is exact
+// in fp32 and needs at most 16 bits, of which mid = bf16(x - hi) keeps 8; the
+// rest, x - hi - mid, needs at most 8 bits and is exact in bf16 (for finite
+// |x| below the largest bf16, about 3.39e38). With q = qh + qm + ql and
+// k = kh + km + kl, six of the nine partial products,
+//     qm.km + ql.kh + qh.kl + qm.kh + qh.km + qh.kh,
+// give q.k up to the three dropped ones (qm.kl, ql.km, ql.kl), at most
+// 2^-23 * sum_c |q_c k_c| in all; each bf16 x bf16 product is exact and the
+// tensor core accumulates in fp32. The small terms go first.
+//
+// Two values a, b -> the bf16 pairs (hi, mid, lo), a in the low halves.
+__device__ __forceinline__ void split3_bf16x2(float a, float b, uint32_t& hi,
+                                              uint32_t& mid, uint32_t& lo) {
+  hi = pack_bf16x2(a, b);
+  const float ra = __fsub_rn(a, __uint_as_float(hi << 16));
+  const float rb = __fsub_rn(b, __uint_as_float(hi & 0xffff0000u));
+  mid = pack_bf16x2(ra, rb);
+  lo = pack_bf16x2(__fsub_rn(ra, __uint_as_float(mid << 16)),
+                   __fsub_rn(rb, __uint_as_float(mid & 0xffff0000u)));
+}
+
+// A tile of R fp32 rows (DP columns, zero beyond d and beyond the first
+// `nvalid` rows) held in registers between a global load and a split store
+// into three bf16 K-major core-matrix planes (hi, mid, lo) of `plane` bytes
+// each. 128 threads; item e = threadIdx.x + 128 u is the 8-element piece
+// (row ((e / 8) / KCH) * 8 + e % 8, chunk (e / 8) % KCH) whose bf16 image
+// sits at byte 16 e of each plane, so the 8 lanes of a shared-memory
+// wavefront write 128 contiguous bytes and a warp reads 16 whole rows.
+// Requires d % 8 == 0 and 16-byte aligned rows (row stride % 4 == 0).
+template <int DP, int R>
+struct SplitTile {
+  static constexpr int KCH = DP / 8;
+  static constexpr int U = R * KCH / 128;
+  static_assert(U >= 1 && (R * KCH) % 128 == 0, "tile shape");
+  float4 x[U][2];
+
+  __device__ __forceinline__ void load(const float* src, int64_t rs,
+                                       int nvalid, int d) {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int e = threadIdx.x + 128 * u;
+      const int r = ((e >> 3) / KCH) * 8 + (e & 7);
+      const int c = (e >> 3) % KCH;
+      if (r < nvalid && c * 8 < d) {
+        const float4* g =
+            reinterpret_cast<const float4*>(src + (int64_t)r * rs + c * 8);
+        x[u][0] = __ldg(g);
+        x[u][1] = __ldg(g + 1);
+      } else {
+        x[u][0] = make_float4(0.f, 0.f, 0.f, 0.f);
+        x[u][1] = x[u][0];
+      }
+    }
+  }
+
+  __device__ __forceinline__ void store(uint32_t base, uint32_t plane) const {
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const uint32_t dst = base + (uint32_t)(threadIdx.x + 128 * u) * 16u;
+      uint32_t h[4], m[4], l[4];
+      split3_bf16x2(x[u][0].x, x[u][0].y, h[0], m[0], l[0]);
+      split3_bf16x2(x[u][0].z, x[u][0].w, h[1], m[1], l[1]);
+      split3_bf16x2(x[u][1].x, x[u][1].y, h[2], m[2], l[2]);
+      split3_bf16x2(x[u][1].z, x[u][1].w, h[3], m[3], l[3]);
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst),
+                   "r"(h[0]), "r"(h[1]), "r"(h[2]), "r"(h[3])
+                   : "memory");
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(dst + plane),
+                   "r"(m[0]), "r"(m[1]), "r"(m[2]), "r"(m[3])
+                   : "memory");
+      asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(
+                       dst + 2 * plane),
+                   "r"(l[0]), "r"(l[1]), "r"(l[2]), "r"(l[3])
+                   : "memory");
+    }
+  }
+};
 
 }  // namespace tc
 }  // namespace tarmac

@@ -1,21 +1,31 @@
-// topk_tc.cu — fused top-k attention for bf16 inputs with the score matrix
-// formed on the fifth-generation tensor cores (tcgen05, TMEM accumulators).
+// topk_tc.cu — fused top-k attention with the score matrix formed on the
+// fifth-generation tensor cores (tcgen05, TMEM accumulators), for bf16 and
+// fp32 inputs.
 //
 // Same function as the other fused top-k kernels (reference:
 // src/kernels/fused_topk_attention.py:211-289, 405-504 and
 // src/kernels/streaming_topk_attention.py:66-179): scores q.k with the
 // diagonal excluded, the k best kept under the lowest- or highest-index tie
-// rule, softmax over them, weighted sum of their V rows. bf16 x bf16 products
-// accumulate in fp32, the reference's "bf16 with fp32 accumulation".
+// rule, softmax over them, weighted sum of their V rows.
+// * bf16 inputs: bf16 x bf16 products accumulate in fp32, the reference's
+//   "bf16 with fp32 accumulation".
+// * fp32 inputs: every Q and K row is split exactly into three bf16 planes
+//   (hi + mid + lo, tc_common.cuh:split3_bf16x2) and six plane products
+//   accumulate in fp32 per score, which reproduces the fp32 dot product to
+//   within about 2^-23 * sum_c |q_c k_c| plus the fp32 accumulation
+//   rounding — the size of an fp32 FFMA dot product's own rounding error,
+//   and well inside the fp32 parity tolerance.
 //
 // One block (4 warps) owns 128 queries of one episode; thread t of warp w
 // owns query row 32*w + t, which is also its tensor-memory (TMEM) lane.
 // * Q (128 x d) is staged once in shared memory as bf16 in the K-major
 //   core-matrix layout (tc_common.cuh); K streams through a ring of key
-//   tiles with 16-byte cp.async, ahead of the scan.
+//   tiles, ahead of the scan: 16-byte cp.async for bf16, and for fp32 a
+//   register prefetch issued before the scan of a round and split into the
+//   three planes after it.
 // * Per round one thread issues tcgen05.mma (M = 128, K = 16 per
 //   instruction) for the round's score tile into TMEM and commits it to an
-//   mbarrier: 128-key rounds in one buffer for d <= 16; for larger d,
+//   mbarrier: 128-key rounds in one buffer for bf16 with d <= 16; otherwise
 //   64-key rounds in two buffers, round r + 1's product issued before round
 //   r is scanned so the tensor core works under the scan. A block holds 128
 //   TMEM columns; up to four blocks share an SM's TMEM.
@@ -29,8 +39,8 @@
 //   chunks, in increasing key order, and keeps the exact k best under the
 //   tie rule.
 // * Softmax over the k retained scores; the V gather-aggregate and the
-//   output store run row-cooperatively (DP/8 lanes per row, 16-byte
-//   coalesced pieces) when the rows allow 16-byte access.
+//   output store run row-cooperatively (16-byte coalesced pieces) when the
+//   rows allow 16-byte access.
 #include "tc_common.cuh"
 #include "topk_chunk.cuh"
 
@@ -41,17 +51,27 @@ constexpr int TC_MIN_SMEM = 50 << 10; // caps residency at 4 blocks per SM
 constexpr int TC_STAGE16 = 1;         // flags: 16-byte Q/K staging copies
 constexpr int TC_COOP_VO = 2;         // flags: row-cooperative V/O moves
 
-// Rounds: 128 keys in one TMEM buffer for d <= 16; 64 keys in two buffers
-// (the next round's product computing under the current scan) above that,
-// where each product is larger. The K ring holds one tile more than the
-// buffers. Both keep the block at 128 TMEM columns.
-__host__ __device__ constexpr int tc_round(int DP) { return DP <= 16 ? 128 : 64; }
-__host__ __device__ constexpr int tc_bufs(int DP) { return DP <= 16 ? 1 : 2; }
+// Rounds: 128 keys in one TMEM buffer for bf16 with d <= 16; 64 keys in two
+// buffers (the next round's product computing under the current scan) where
+// each product is larger: bf16 with d > 16, and fp32 (six plane products
+// per K step). The K ring holds one tile more than the buffers. Both keep
+// the block at 128 TMEM columns.
+__host__ __device__ constexpr int tc_round(int DP, bool f32) {
+  return (DP <= 16 && !f32) ? 128 : 64;
+}
+__host__ __device__ constexpr int tc_bufs(int DP, bool f32) {
+  return (DP <= 16 && !f32) ? 1 : 2;
+}
+// bf16 planes per operand: one, or hi / mid / lo for fp32
+__host__ __device__ constexpr int tc_planes(bool f32) { return f32 ? 3 : 1; }
 
-// keys per chunk for a list of KC chunks: the saved scores take 64 floats
-// per row (32 for KC = 1)
-__host__ __device__ constexpr int tc_chunk(int KC) {
-  return KC <= 2 ? 32 : (KC == 4 ? 16 : 8);
+// keys per chunk for a list of KC chunks. bf16: the saved scores take 64
+// floats per row (32 for KC = 1). fp32: 32 floats per row up to KC = 4 (64
+// at KC = 8), which keeps the larger operand planes within four blocks per
+// SM and halves pass 2 at k <= 2.
+__host__ __device__ constexpr int tc_chunk(int KC, bool f32) {
+  return f32 ? (KC == 1 ? 32 : (KC == 2 ? 16 : 8))
+             : (KC <= 2 ? 32 : (KC == 4 ? 16 : 8));
 }
 
 // Insert chunk (cm, cid) into the descending list (mv, mc, ms) of KC chunks
@@ -76,22 +96,24 @@ __device__ __forceinline__ void chunk_insert(float (&mv)[KC], int (&mc)[KC],
   }
 }
 
-template <int DP, int KC, bool TIE_HIGH>
+template <typename T, int DP, int KC, bool TIE_HIGH>
 __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     topk_tc_kernel(AttnParams p, int flags) {
-  using T = __nv_bfloat16;
+  constexpr bool F32 = sizeof(T) == 4;
   constexpr int KCH = DP / 8;  // 16-byte chunks per bf16 row
-  constexpr int RK = tc_round(DP);
-  constexpr int NB = tc_bufs(DP);      // TMEM score buffers
-  constexpr int TC_SLOTS = NB + 1;     // K ring depth
-  constexpr int QBYTES = 128 * DP * 2;
-  constexpr int TILE_BYTES = RK * DP * 2;
-  constexpr int CH = tc_chunk(KC);
+  constexpr int RK = tc_round(DP, F32);
+  constexpr int NB = tc_bufs(DP, F32);  // TMEM score buffers
+  constexpr int TC_SLOTS = NB + 1;      // K ring depth
+  constexpr int PL = tc_planes(F32);
+  constexpr int QPLANE = 128 * DP * 2;  // bytes of one Q plane
+  constexpr int KPLANE = RK * DP * 2;   // bytes of one K plane of a tile
+  constexpr int TILE_BYTES = PL * KPLANE;
+  constexpr int CH = tc_chunk(KC, F32);
   constexpr int G = CH / 4;    // float4 groups per chunk
   constexpr int RG = KC * G;   // float4 groups per row's slots
   extern __shared__ __align__(16) unsigned char tc_smem[];
-  unsigned char* sQ = tc_smem;                  // 128 x DP bf16
-  unsigned char* sK = sQ + QBYTES;              // TC_SLOTS x RK x DP bf16
+  unsigned char* sQ = tc_smem;               // PL planes of 128 x DP bf16
+  unsigned char* sK = sQ + PL * QPLANE;      // TC_SLOTS x PL x RK x DP bf16
   // saved chunks: row r's KC slots at sv + r * (RG + 1); the one-float4 pad
   // puts the 8 lanes of a 128-byte wavefront on 8 distinct bank groups
   float4* sv = reinterpret_cast<float4*>(sK + TC_SLOTS * TILE_BYTES);
@@ -112,24 +134,44 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
   const T* V = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
   T* O = static_cast<T*>(p.o) + (int64_t)b * p.st.ob;
 
-  // K rows [r0, r0 + RK) into ring slot sl
-  auto stage_k = [&](int sl, int r0) {
-    if (vec16)
-      tc::stage_fast<DP, RK, false>(tc::smem_addr(sK) + sl * TILE_BYTES,
-                                    K + (int64_t)r0 * p.st.kn, p.st.kn, N - r0,
-                                    d);
-    else
-      tc::stage_kmajor<DP>(sK + sl * TILE_BYTES, K, p.st.kn, r0, RK, N, d,
-                           false);
-  };
   const int rounds = cdiv(N, RK);
-  if (vec16)
-    tc::stage_fast<DP, 128, false>(tc::smem_addr(sQ), Q + (int64_t)q0 * p.st.qn,
-                                   p.st.qn, N - q0, d);
-  else
-    tc::stage_kmajor<DP>(sQ, Q, p.st.qn, q0, 128, N, d, false);
-  stage_k(0, 0);
-  if (NB == 2 && rounds > 1) stage_k(1, RK);
+  // K rows [r0, r0 + RK) into ring slot sl (bf16: cp.async or element copies)
+  auto stage_k = [&](int sl, int r0) {
+    if constexpr (!F32) {
+      if (vec16)
+        tc::stage_fast<DP, RK, false>(tc::smem_addr(sK) + sl * TILE_BYTES,
+                                      K + (int64_t)r0 * p.st.kn, p.st.kn,
+                                      N - r0, d);
+      else
+        tc::stage_kmajor<DP>(sK + sl * TILE_BYTES, K, p.st.kn, r0, RK, N, d,
+                             false);
+    }
+  };
+  // fp32: the next K tile in registers, loaded before a round's scan and
+  // split into its ring slot after it
+  tc::SplitTile<DP, RK> kpre;
+  if constexpr (F32) {
+    const float* Qf = reinterpret_cast<const float*>(Q);
+    const float* Kf = reinterpret_cast<const float*>(K);
+    tc::SplitTile<DP, 128> qt;
+    qt.load(Qf + (int64_t)q0 * p.st.qn, p.st.qn, N - q0, d);
+    kpre.load(Kf, p.st.kn, N, d);
+    qt.store(tc::smem_addr(sQ), QPLANE);
+    kpre.store(tc::smem_addr(sK), KPLANE);
+    if (rounds > 1) {
+      kpre.load(Kf + (int64_t)RK * p.st.kn, p.st.kn, N - RK, d);
+      kpre.store(tc::smem_addr(sK) + TILE_BYTES, KPLANE);
+    }
+  } else {
+    if (vec16)
+      tc::stage_fast<DP, 128, false>(tc::smem_addr(sQ),
+                                     Q + (int64_t)q0 * p.st.qn, p.st.qn,
+                                     N - q0, d);
+    else
+      tc::stage_kmajor<DP>(sQ, Q, p.st.qn, q0, 128, N, d, false);
+    stage_k(0, 0);
+    if (NB == 2 && rounds > 1) stage_k(1, RK);
+  }
   if (warp == 0) tc::tmem_alloc(&tmem_sh, NB * RK);
   if (threadIdx.x == 0) {
     tc::mbar_init(&mbar[0], 1);
@@ -160,10 +202,27 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     const uint32_t kt = ka + (uint32_t)((r % TC_SLOTS) * TILE_BYTES);
     const uint32_t idesc = tc::idesc_bf16(128, nt, false, false);
 #pragma unroll
-    for (int ks = 0; ks < DP / 16; ++ks)
-      tc::mma_bf16(tmem + (r % NB) * RK,
-                   tc::smem_desc(qa + ks * 256, 128, KCH * 128),
-                   tc::smem_desc(kt + ks * 256, 128, KCH * 128), idesc, ks > 0);
+    for (int ks = 0; ks < DP / 16; ++ks) {
+      if constexpr (F32) {
+        // plane products, small terms first: m.m, l.h, h.l, m.h, h.m, h.h
+        // (plane 0 = hi, 1 = mid, 2 = lo; A = Q, B = K)
+        constexpr int PA[6] = {1, 2, 0, 1, 0, 0};
+        constexpr int PB[6] = {1, 0, 2, 0, 1, 0};
+#pragma unroll
+        for (int t = 0; t < 6; ++t)
+          tc::mma_bf16(tmem + (r % NB) * RK,
+                       tc::smem_desc(qa + PA[t] * QPLANE + ks * 256, 128,
+                                     KCH * 128),
+                       tc::smem_desc(kt + PB[t] * KPLANE + ks * 256, 128,
+                                     KCH * 128),
+                       idesc, ks > 0 || t > 0);
+      } else {
+        tc::mma_bf16(tmem + (r % NB) * RK,
+                     tc::smem_desc(qa + ks * 256, 128, KCH * 128),
+                     tc::smem_desc(kt + ks * 256, 128, KCH * 128), idesc,
+                     ks > 0);
+      }
+    }
     tc::mma_commit(&mbar[r % NB]);
   };
 
@@ -185,7 +244,14 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
       if (NB == 1 && r > 0) issue(r);
     }
     // slot (r + NB) % TC_SLOTS last held tile r - 1, whose product completed
-    if (r + NB < rounds) stage_k((r + NB) % TC_SLOTS, (r + NB) * RK);
+    if constexpr (F32) {
+      if (r + NB < rounds)
+        kpre.load(reinterpret_cast<const float*>(K) +
+                      (int64_t)(r + NB) * RK * p.st.kn,
+                  p.st.kn, N - (r + NB) * RK, d);
+    } else {
+      if (r + NB < rounds) stage_k((r + NB) % TC_SLOTS, (r + NB) * RK);
+    }
     ok &= tc::mbar_wait(&mbar[r % NB], (uint32_t)((r / NB) & 1));
     tc::fence_after_sync();
 
@@ -223,6 +289,10 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
           }
         }
       }
+    }
+    if constexpr (F32) {
+      if (r + NB < rounds)
+        kpre.store(ka + (uint32_t)(((r + NB) % TC_SLOTS) * TILE_BYTES), KPLANE);
     }
   }
   tc::fence_before_sync();
@@ -290,8 +360,8 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     float w[KC];
 #pragma unroll
     for (int m = 0; m < KC; ++m) w[m] = (m < kk) ? e[m] / den : 0.f;
-    tc::coop_gather_store<DP, KC>(V, p.st.vn, O, p.st.on, q0 + warp * 32, N, d,
-                                  kk, bi, w, empty);
+    tc::coop_gather_store<T, DP, KC>(V, p.st.vn, O, p.st.on, q0 + warp * 32,
+                                     N, d, kk, bi, w, empty);
     return;
   }
   if (i >= N) return;
@@ -331,30 +401,37 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
   store_row<DP, T>(O + (int64_t)i * p.st.on, acc, d, vec);
 }
 
-template <int DP, int KC, bool TIE_HIGH>
+template <typename T, int DP, int KC, bool TIE_HIGH>
 static cudaError_t launch_tc_t(const AttnParams& p, int flags, cudaStream_t s) {
-  const size_t need = (size_t)(128 + (tc_bufs(DP) + 1) * tc_round(DP)) * DP * 2 +
-                      (size_t)128 * (KC * tc_chunk(KC) + 4) * 4;
+  constexpr bool F32 = sizeof(T) == 4;
+  const size_t need =
+      (size_t)tc_planes(F32) *
+          (128 + (tc_bufs(DP, F32) + 1) * tc_round(DP, F32)) * DP * 2 +
+      (size_t)128 * (KC * tc_chunk(KC, F32) + 4) * 4;
   const size_t sm = need > (size_t)TC_MIN_SMEM ? need : (size_t)TC_MIN_SMEM;
-  cudaError_t e = cudaFuncSetAttribute(topk_tc_kernel<DP, KC, TIE_HIGH>,
+  cudaError_t e = cudaFuncSetAttribute(topk_tc_kernel<T, DP, KC, TIE_HIGH>,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sm);
   if (e != cudaSuccess) return e;
   const int64_t blocks = (int64_t)p.B * cdiv(p.N, 128);
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  topk_tc_kernel<DP, KC, TIE_HIGH>
+  topk_tc_kernel<T, DP, KC, TIE_HIGH>
       <<<(unsigned)blocks, TC_THREADS, sm, s>>>(p, flags);
   return cudaGetLastError();
 }
 
-template <int DP, bool TIE_HIGH>
+template <typename T, int DP, bool TIE_HIGH>
 static cudaError_t launch_tc_kc(const AttnParams& p, int flags, cudaStream_t s) {
   switch (chunk_slots(p.topk)) {
-    case 1: return launch_tc_t<DP, 1, TIE_HIGH>(p, flags, s);
-    case 2: return launch_tc_t<DP, 2, TIE_HIGH>(p, flags, s);
-    case 4: return launch_tc_t<DP, 4, TIE_HIGH>(p, flags, s);
-    default: return launch_tc_t<DP, 8, TIE_HIGH>(p, flags, s);
+    case 1: return launch_tc_t<T, DP, 1, TIE_HIGH>(p, flags, s);
+    case 2: return launch_tc_t<T, DP, 2, TIE_HIGH>(p, flags, s);
+    case 4: return launch_tc_t<T, DP, 4, TIE_HIGH>(p, flags, s);
+    default: return launch_tc_t<T, DP, 8, TIE_HIGH>(p, flags, s);
   }
+}
+
+static bool a16(const void* x) {
+  return reinterpret_cast<uintptr_t>(x) % 16 == 0;
 }
 
 // bf16, N >= 128, k <= 8: is the tensor-core top-k path available?
@@ -363,9 +440,7 @@ bool topk_tc_supported(const AttnParams& p) {
 }
 
 cudaError_t launch_topk_tc(const AttnParams& p, bool tie_high, cudaStream_t s) {
-  const auto a16 = [](const void* x) {
-    return reinterpret_cast<uintptr_t>(x) % 16 == 0;
-  };
+  using B16 = __nv_bfloat16;
   const bool d8 = p.d % 8 == 0;
   // 16-byte staging copies of Q and K; 16-byte row moves of V and O
   const bool qk = d8 && a16(p.q) && a16(p.k) && p.st.qn % 8 == 0 &&
@@ -375,11 +450,30 @@ cudaError_t launch_topk_tc(const AttnParams& p, bool tie_high, cudaStream_t s) {
   const int flags = (qk ? TC_STAGE16 : 0) | (vo ? TC_COOP_VO : 0);
   const int dp = p.d <= 16 ? 16 : p.d <= 32 ? 32 : p.d <= 64 ? 64 : 128;
   switch (dp) {
-    case 16: return tie_high ? launch_tc_kc<16, true>(p, flags, s) : launch_tc_kc<16, false>(p, flags, s);
-    case 32: return tie_high ? launch_tc_kc<32, true>(p, flags, s) : launch_tc_kc<32, false>(p, flags, s);
-    case 64: return tie_high ? launch_tc_kc<64, true>(p, flags, s) : launch_tc_kc<64, false>(p, flags, s);
-    default: return tie_high ? launch_tc_kc<128, true>(p, flags, s) : launch_tc_kc<128, false>(p, flags, s);
+    case 16: return tie_high ? launch_tc_kc<B16, 16, true>(p, flags, s) : launch_tc_kc<B16, 16, false>(p, flags, s);
+    case 32: return tie_high ? launch_tc_kc<B16, 32, true>(p, flags, s) : launch_tc_kc<B16, 32, false>(p, flags, s);
+    case 64: return tie_high ? launch_tc_kc<B16, 64, true>(p, flags, s) : launch_tc_kc<B16, 64, false>(p, flags, s);
+    default: return tie_high ? launch_tc_kc<B16, 128, true>(p, flags, s) : launch_tc_kc<B16, 128, false>(p, flags, s);
   }
+}
+
+// fp32, N >= 128, d a multiple of 8 up to 16, k <= 8, 16-byte aligned rows
+// (Q and K rows are loaded as 16-byte pieces and split into bf16 planes; V
+// and O rows move as 16-byte pieces): is the split tensor-core path
+// available?
+bool topk_tc_f32_supported(const AttnParams& p) {
+  if (p.N < 128 || p.d > 16 || p.d % 8 != 0 || p.topk > 8) return false;
+  const Strides& t = p.st;
+  return a16(p.q) && a16(p.k) && a16(p.v) && a16(p.o) && t.qn % 4 == 0 &&
+         t.kn % 4 == 0 && t.vn % 4 == 0 && t.on % 4 == 0 && t.qb % 4 == 0 &&
+         t.kb % 4 == 0 && t.vb % 4 == 0 && t.ob % 4 == 0;
+}
+
+cudaError_t launch_topk_tc_f32(const AttnParams& p, bool tie_high,
+                               cudaStream_t s) {
+  const int flags = TC_STAGE16 | TC_COOP_VO;
+  return tie_high ? launch_tc_kc<float, 16, true>(p, flags, s)
+                  : launch_tc_kc<float, 16, false>(p, flags, s);
 }
 
 }  // namespace tarmac
