@@ -51,7 +51,7 @@ def log(*a) -> None:
 def _profiled_traffic() -> float | None:
     """DRAM bytes (read + write) of one top-k launch at this workload, from the
     committed ncu summary (line ``traffic_bytes_per_launch: N``)."""
-    f = REPO / "profiles" / "topk_chunk_c2.md"
+    f = REPO / "profiles" / "topk_tc_f32_c2.md"
     if not f.exists():
         return None
     import re
@@ -514,6 +514,10 @@ def run_ours(args) -> int:
     peaks = _peaks()
     alg_bytes = 4 * B * N * d * 4                      # q, k, v read; out written
     alg_flops = 2 * B * N * N * d + 2 * B * N * k * d  # scores + aggregation
+    # the kernel forms each fp32 score as six bf16 plane products on the
+    # tensor cores (hi/mid/lo split of q and k): tensor flops executed
+    tc_flops = 6 * 2 * B * N * N * d
+    achieved_tc = tc_flops / (kernel_ms * 1e-3) / 1e12
     achieved_gbs = alg_bytes / (kernel_ms * 1e-3) / 1e9
     achieved_tf = alg_flops / (kernel_ms * 1e-3) / 1e12
     line = {
@@ -542,11 +546,18 @@ def run_ours(args) -> int:
                      "traffic": (args.traffic if args.traffic is not None
                                  else _profiled_traffic()),
                      "peak_src": peaks["src"]},
-        "roofline_compute": {"bound": "fp32_ffma", "achieved": achieved_tf,
-                             "peak": fp32_tf, "unit": "TFLOP/s",
-                             "frac": achieved_tf / fp32_tf if fp32_tf else None,
-                             "peak_src": "measured: cuBLAS fp32 GEMM 8192^3, "
-                                         "TF32 off, this run"},
+        "roofline_compute": {"bound": "tensor", "achieved": achieved_tc,
+                             "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": achieved_tc / peaks["bf16_tflops"],
+                             "flops_per_launch": tc_flops,
+                             "note": "bf16 tensor flops executed: six plane "
+                                     "products (exact hi/mid/lo split of the "
+                                     "fp32 q and k) per score",
+                             "peak_src": f"{peaks['src']}: bf16 GEMM burst",
+                             "fp32_equivalent_tflops": achieved_tf,
+                             "fp32_simt_gemm_tflops": fp32_tf,
+                             "fp32_simt_src": "measured: cuBLAS fp32 GEMM "
+                                              "8192^3, TF32 off, this run"},
         "clocks": clk.summary(),
         "sweep_c2_us": sweep,
         "sweep_c5_bf16": sweep_c5,

@@ -25,10 +25,10 @@
 //   three planes after it.
 // * Per round one thread issues tcgen05.mma (M = 128, K = 16 per
 //   instruction) for the round's score tile into TMEM and commits it to an
-//   mbarrier: 128-key rounds in one buffer for bf16 with d <= 16; otherwise
-//   64-key rounds in two buffers, round r + 1's product issued before round
-//   r is scanned so the tensor core works under the scan. A block holds 128
-//   TMEM columns; up to four blocks share an SM's TMEM.
+//   mbarrier: 128-key rounds in one buffer for d <= 16; otherwise 64-key
+//   rounds in two buffers, round r + 1's product issued before round r is
+//   scanned so the tensor core works under the scan. A block holds 128 TMEM
+//   columns; up to four blocks share an SM's TMEM.
 // * Pass 1 (per round): every thread reads its row's scores (tcgen05.ld, 32
 //   columns at a time), forms the maximum of each chunk of CH keys and keeps
 //   the KC >= k best chunks (the k best scores lie in them). A chunk that
@@ -51,17 +51,15 @@ constexpr int TC_MIN_SMEM = 50 << 10; // caps residency at 4 blocks per SM
 constexpr int TC_STAGE16 = 1;         // flags: 16-byte Q/K staging copies
 constexpr int TC_COOP_VO = 2;         // flags: row-cooperative V/O moves
 
-// Rounds: 128 keys in one TMEM buffer for bf16 with d <= 16; 64 keys in two
-// buffers (the next round's product computing under the current scan) where
-// each product is larger: bf16 with d > 16, and fp32 (six plane products
-// per K step). The K ring holds one tile more than the buffers. Both keep
-// the block at 128 TMEM columns.
-__host__ __device__ constexpr int tc_round(int DP, bool f32) {
-  return (DP <= 16 && !f32) ? 128 : 64;
-}
-__host__ __device__ constexpr int tc_bufs(int DP, bool f32) {
-  return (DP <= 16 && !f32) ? 1 : 2;
-}
+// Rounds: 128 keys in one TMEM buffer for d <= 16 (fewer rounds, so fewer
+// block barriers; the other blocks on the SM run while one waits for its
+// product — for fp32 this measured faster than 64-key rounds in two buffers
+// despite the six plane products); 64 keys in two buffers (the next round's
+// product computing under the current scan) for d > 16, where each product
+// is larger. The K ring holds one tile more than the buffers. Both keep the
+// block at 128 TMEM columns.
+__host__ __device__ constexpr int tc_round(int DP) { return DP <= 16 ? 128 : 64; }
+__host__ __device__ constexpr int tc_bufs(int DP) { return DP <= 16 ? 1 : 2; }
 // bf16 planes per operand: one, or hi / mid / lo for fp32
 __host__ __device__ constexpr int tc_planes(bool f32) { return f32 ? 3 : 1; }
 
@@ -101,8 +99,8 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     topk_tc_kernel(AttnParams p, int flags) {
   constexpr bool F32 = sizeof(T) == 4;
   constexpr int KCH = DP / 8;  // 16-byte chunks per bf16 row
-  constexpr int RK = tc_round(DP, F32);
-  constexpr int NB = tc_bufs(DP, F32);  // TMEM score buffers
+  constexpr int RK = tc_round(DP);
+  constexpr int NB = tc_bufs(DP);  // TMEM score buffers
   constexpr int TC_SLOTS = NB + 1;      // K ring depth
   constexpr int PL = tc_planes(F32);
   constexpr int QPLANE = 128 * DP * 2;  // bytes of one Q plane
@@ -158,7 +156,7 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
     kpre.load(Kf, p.st.kn, N, d);
     qt.store(tc::smem_addr(sQ), QPLANE);
     kpre.store(tc::smem_addr(sK), KPLANE);
-    if (rounds > 1) {
+    if (NB == 2 && rounds > 1) {
       kpre.load(Kf + (int64_t)RK * p.st.kn, p.st.kn, N - RK, d);
       kpre.store(tc::smem_addr(sK) + TILE_BYTES, KPLANE);
     }
@@ -406,7 +404,7 @@ static cudaError_t launch_tc_t(const AttnParams& p, int flags, cudaStream_t s) {
   constexpr bool F32 = sizeof(T) == 4;
   const size_t need =
       (size_t)tc_planes(F32) *
-          (128 + (tc_bufs(DP, F32) + 1) * tc_round(DP, F32)) * DP * 2 +
+          (128 + (tc_bufs(DP) + 1) * tc_round(DP)) * DP * 2 +
       (size_t)128 * (KC * tc_chunk(KC, F32) + 4) * 4;
   const size_t sm = need > (size_t)TC_MIN_SMEM ? need : (size_t)TC_MIN_SMEM;
   cudaError_t e = cudaFuncSetAttribute(topk_tc_kernel<T, DP, KC, TIE_HIGH>,
