@@ -284,6 +284,85 @@ def _sweep_c5(ops, dev, stream) -> list:
     return rows
 
 
+def _sweep_c3(ops, dev, stream) -> list:
+    """BASELINE configs[2], streaming top-k at large N: B=256, N in {512,
+    768, 1024}, d=16, k in {1, 2, 4}, fp32 and bf16 inputs, through the
+    streaming entry point. Informational (warm: the inputs fit L2; 20 reps
+    after one warm-up call)."""
+    import torch
+    rows = []
+    B, d = 256, 16
+    for n_ in (512, 768, 1024):
+        gs = torch.Generator().manual_seed(1234 + 7 * n_ + d)
+        q_, k_, v_ = (torch.randn(B, n_, d, generator=gs).to(dev) for _ in range(3))
+        row = {"B": B, "N": n_, "d": d}
+        for tag, (a, b, c) in (("f32", (q_, k_, v_)),
+                               ("bf16", tuple(x.to(torch.bfloat16)
+                                              for x in (q_, k_, v_)))):
+            for kk_ in (1, 2, 4):
+                ops.streaming_topk_attention(a, b, c, kk_)
+                t = _time_loop(lambda s: ops.streaming_topk_attention(a, b, c, kk_),
+                               20, stream) / 20
+                row[f"{tag}_k{kk_}_us"] = round(1e3 * t, 2)
+        rows.append(row)
+        del q_, k_, v_
+    return rows
+
+
+def _sweep_c4(ops, dev, stream) -> list:
+    """BASELINE configs[3], select-before-scoring: N in {64, 256, 512}, k=2,
+    16-bit-per-axis Morton window, d=16 fp32 attention over the N*k pairs, at
+    B=1024 (the config) and B=4096. Per point: the fused selector+attention
+    kernel (no index tensor), and the two-launch form (selector writing int64
+    indices, then the prescore kernel). Inputs rotate over sets larger than
+    L2 in total; HBM fraction of the fused kernel from its algorithmic bytes
+    B*N*(8 + 4*d*4) (positions read, Q/K/V read, O written)."""
+    import torch
+    peaks = _peaks()
+    rows = []
+    d, kk_, bits = 16, 2, 16
+    for B in (1024, 4096):
+        for n_ in (64, 256, 512):
+            per_set = B * n_ * (3 * d * 4 + 8)
+            nsets = max(2, -(-(300 << 20) // per_set))
+            gs = torch.Generator().manual_seed(4242 + n_)
+            sets_ = []
+            for _ in range(nsets):
+                q_, k_, v_ = (torch.randn(B, n_, d, generator=gs).to(dev)
+                              for _ in range(3))
+                pos_ = torch.rand(B, n_, 2, generator=gs).to(dev)
+                sets_.append((q_, k_, v_, pos_))
+            reps = 20
+
+            def fused(s):
+                q_, k_, v_, pos_ = sets_[s % nsets]
+                ops.morton_prescore_attention(q_, k_, v_, pos_, kk_, bits=bits)
+
+            def two_step(s):
+                q_, k_, v_, pos_ = sets_[s % nsets]
+                idx = ops.morton_select(pos_, kk_, bits=bits)
+                ops.prescore_attention(q_, k_, v_, idx)
+
+            def select_only(s):
+                ops.morton_select(sets_[s % nsets][3], kk_, bits=bits)
+
+            row = {"B": B, "N": n_, "d": d, "k": kk_, "bits": bits}
+            for name, fn in (("fused_us", fused), ("select_plus_prescore_us", two_step),
+                             ("select_us", select_only)):
+                for s in range(3):
+                    fn(s)
+                t = _time_loop(fn, reps, stream) / reps
+                row[name] = round(1e3 * t, 2)
+            byts = B * n_ * (8 + 4 * d * 4)
+            gbs = byts / (row["fused_us"] * 1e-6) / 1e9
+            row["fused_hbm_gbs"] = round(gbs, 1)
+            row["fused_hbm_frac"] = round(gbs / peaks["hbm_gbs"], 3)
+            row["fused_agent_rows_per_s"] = B * n_ / (row["fused_us"] * 1e-6)
+            rows.append(row)
+            del sets_
+    return rows
+
+
 def _comm_c1(ops, dev, stream) -> dict:
     """BASELINE configs[0] shape through the whole comm module forward (qkv
     Linear -> top-k core -> GELU -> proj), B=256, N=6, in_dim=64, msg_dim=16,
@@ -502,6 +581,8 @@ def run_ours(args) -> int:
             sweep.append(row)
         del q_, k_, v_
     sweep_c5 = _sweep_c5(ops, dev, stream) if rank == 0 and not args.no_sweep else []
+    sweep_c3 = _sweep_c3(ops, dev, stream) if rank == 0 and not args.no_sweep else []
+    sweep_c4 = _sweep_c4(ops, dev, stream) if rank == 0 and not args.no_sweep else []
     comm_c1 = _comm_c1(ops, dev, stream) if rank == 0 and not args.no_sweep else {}
 
     fp32_tf = _fp32_peak(dev) if rank == 0 else None
@@ -561,6 +642,8 @@ def run_ours(args) -> int:
         "clocks": clk.summary(),
         "sweep_c2_us": sweep,
         "sweep_c5_bf16": sweep_c5,
+        "sweep_c3_stream_us": sweep_c3,
+        "sweep_c4_zorder": sweep_c4,
         "comm_module_c1": comm_c1,
     }
     if world == 1 and not args.no_cpu:

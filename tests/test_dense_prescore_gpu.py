@@ -101,6 +101,34 @@ def test_morton_window_bit_exact(ops, N, k, bits):
     np.testing.assert_array_equal(got, oracle.morton_window(pos.numpy(), k, bits))
 
 
+@pytest.mark.parametrize("N", [31, 32, 33, 65, 127, 129, 255, 257, 511, 512,
+                               513, 1023, 1024, 1025])
+def test_morton_window_sort_tiers_and_equal_codes(ops, N):
+    """Episode sizes at the edges of the register-sort tiers (32 to 1024
+    keys over up to 4 warps, up to 8 per lane; the shared-memory sort above
+    1024), with duplicated
+    positions (equal codes keep index order), a collapsed episode (every
+    code 0) and a collapsed axis; selector and fused kernel both follow the
+    stable order."""
+    g = torch.Generator().manual_seed(N)
+    pos = torch.rand(8, N, 2, generator=g)
+    pos[0, N // 2:] = pos[0, : N - N // 2].clone()
+    pos[1] = 0.5
+    pos[2, :, 0] = 0.25
+    q, kt, v = qkv(8, N, 16, seed=N + 1)
+    for k, bits in ((1, 16), (2, 16), (3, 10)):
+        if k >= N:
+            continue
+        want = oracle.morton_window(pos.numpy(), k, bits)
+        got = ops.morton_select(pos.cuda(), k, bits).cpu().numpy()
+        np.testing.assert_array_equal(got, want)
+        out, idx = ops.morton_prescore_attention(q, kt, v, pos.cuda(), k, bits,
+                                                 return_indices=True)
+        np.testing.assert_array_equal(idx.cpu().numpy(), want)
+        ref = oracle.prescore_attention(host(q), host(kt), host(v), want)
+        np.testing.assert_allclose(host(out), ref, rtol=1e-5, atol=1e-5)
+
+
 @pytest.mark.parametrize("N,d,kk,itype", [(64, 16, 2, torch.int64),
                                           (512, 16, 2, torch.int32),
                                           (100, 8, 5, torch.int64),

@@ -191,6 +191,22 @@ __device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gsrc)
                : "memory");
 }
+// cp.async of 16 bytes to a shared-memory address (as a 32-bit shared
+// window offset)
+__device__ __forceinline__ void cp_async16_addr(uint32_t smem_dst,
+                                                const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_dst),
+               "l"(gsrc)
+               : "memory");
+}
+__device__ __forceinline__ void st_shared_zero16(uint32_t smem_dst) {
+  asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(smem_dst),
+               "r"(0u)
+               : "memory");
+}
+__device__ __forceinline__ uint32_t tc_smem_base(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
 }

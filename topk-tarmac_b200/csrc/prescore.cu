@@ -6,10 +6,12 @@
 // accumulator) and write only the result. The eager counterpart is
 // prescore_attention (src/kernels/prescore_selection.py:442-453).
 //
-// Layout: a row is handled by a group of L = DP/4 lanes, each owning 4
-// consecutive columns, so Q/O accesses are fully coalesced 16-byte vectors and
-// each gathered K/V row is fetched as L contiguous 16-byte pieces. The
-// partial dot products meet in log2(L) butterfly shuffles.
+// Layout: d <= 16: one thread per query row (its softmax runs once; the
+// peers' K and V rows are loaded two peers at a time before the scores).
+// Wider rows: a group of L = DP/4 lanes, each owning 4 consecutive columns,
+// so Q/O accesses are fully coalesced 16-byte vectors and each gathered K/V
+// row is fetched as L contiguous 16-byte pieces; the partial dot products
+// meet in log2(L) butterfly shuffles.
 #include "prescore.cuh"
 
 namespace tarmac {
@@ -32,14 +34,70 @@ __global__ void __launch_bounds__(256) prescore_kernel(AttnParams p,
   PrescoreRow<DP, T> pr;
   pr.init(p, b, i, sub, live);
   bool bad = false;
-#pragma unroll 4
-  for (int j = 0; j < kk; ++j) {
-    const int64_t pj = live ? (int64_t)ir[j] : 0;
-    const bool ok = pj >= 0 && pj < N;
-    bad |= !ok;
-    pr.step(p, b, ok ? (int)pj : 0, sub);
+  // peers in groups of four: the group's indices, then its K and V rows, are
+  // loaded together
+  for (int j0 = 0; j0 < kk; j0 += 4) {
+    const int cnt = min(4, kk - j0);
+    int js[4];
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const int64_t pj = (live && m < cnt) ? (int64_t)ir[j0 + m] : 0;
+      const bool ok = pj >= 0 && pj < N;
+      bad |= !ok;
+      js[m] = ok ? (int)pj : 0;
+    }
+    pr.template steps<4>(p, b, js, cnt, sub);
   }
   if (live) pr.finish(p, b, i, sub, bad);
+}
+
+// d <= DT (8 or 16): one query row per thread; the peers' indices, then
+// their K and V rows, two peers at a time.
+template <int DT, typename T, typename I>
+__global__ void __launch_bounds__(256) prescore_thread_kernel(
+    AttnParams p, const I* __restrict__ idx, int kk) {
+  const int64_t row = (int64_t)blockIdx.x * 256 + threadIdx.x;
+  if (row >= (int64_t)p.B * p.N) return;
+  const int N = p.N;
+  const int b = (int)(row / N);
+  const int i = (int)(row - (int64_t)b * N);
+  const T* Kb = static_cast<const T*>(p.k) + (int64_t)b * p.st.kb;
+  const T* Vb = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
+  PrescoreRowThread<DT, T> pr;
+  pr.init(p, static_cast<const T*>(p.q) + (int64_t)b * p.st.qb +
+                 (int64_t)i * p.st.qn,
+          true);
+  const I* ir = idx + row * kk;
+  bool bad = false;
+  for (int j0 = 0; j0 < kk; j0 += 2) {
+    const int cnt = min(2, kk - j0);
+    const T* kr[2];
+    const T* vr[2];
+#pragma unroll
+    for (int m = 0; m < 2; ++m) {
+      const int64_t pj = m < cnt ? (int64_t)ir[j0 + m] : 0;
+      const bool ok = pj >= 0 && pj < N;
+      bad |= !ok;
+      const int64_t j = ok ? pj : 0;
+      kr[m] = Kb + j * p.st.kn;
+      vr[m] = Vb + j * p.st.vn;
+    }
+    pr.steps2(p, kr, vr, cnt);
+  }
+  pr.finish(p, static_cast<T*>(p.o) + (int64_t)b * p.st.ob +
+                   (int64_t)i * p.st.on,
+            bad);
+}
+
+template <int DT, typename T, typename I>
+static cudaError_t launch_prescore_thread(const AttnParams& p, const void* idx,
+                                          int kk, cudaStream_t s) {
+  const int64_t rows = (int64_t)p.B * p.N;
+  const int64_t blocks = (rows + 255) / 256;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  prescore_thread_kernel<DT, T, I><<<(unsigned)blocks, 256, 0, s>>>(
+      p, static_cast<const I*>(idx), kk);
+  return cudaGetLastError();
 }
 
 template <int DP, typename T, typename I>
@@ -57,8 +115,8 @@ static cudaError_t launch_prescore_t(const AttnParams& p, const void* idx,
 template <typename T, typename I>
 static cudaError_t launch_prescore_ti(const AttnParams& p, const void* idx,
                                       int kk, cudaStream_t s) {
-  if (p.d <= 8) return launch_prescore_t<8, T, I>(p, idx, kk, s);
-  if (p.d <= 16) return launch_prescore_t<16, T, I>(p, idx, kk, s);
+  if (p.d <= 8) return launch_prescore_thread<8, T, I>(p, idx, kk, s);
+  if (p.d <= 16) return launch_prescore_thread<16, T, I>(p, idx, kk, s);
   if (p.d <= 32) return launch_prescore_t<32, T, I>(p, idx, kk, s);
   if (p.d <= 64) return launch_prescore_t<64, T, I>(p, idx, kk, s);
   return launch_prescore_t<128, T, I>(p, idx, kk, s);

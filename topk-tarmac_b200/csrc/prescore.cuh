@@ -56,6 +56,39 @@ struct PrescoreRow {
                   (int64_t)j * p.st.vn;
     const float4 kv = load_cols4<T>(kr, sub * 4, p.d, vec);
     const float4 vv = load_cols4<T>(vr, sub * 4, p.d, vec);
+    apply(p, kv, vv);
+  }
+
+  // Up to G peers js[0..cnt) (range-checked) in order: every K and V piece
+  // is loaded before the first score is formed, so a row waits for one
+  // memory round trip per G peers instead of one per peer; the online
+  // softmax then takes them in the same order as step(). Every lane of the
+  // warp must call it with the same cnt.
+  template <int G>
+  __device__ __forceinline__ void steps(const AttnParams& p, int b,
+                                        const int (&js)[G], int cnt,
+                                        int sub) {
+    const bool vec = p.vec != 0;
+    float4 kv[G], vv[G];
+#pragma unroll
+    for (int m = 0; m < G; ++m) {
+      if (m < cnt) {
+        const T* kr = static_cast<const T*>(p.k) + (int64_t)b * p.st.kb +
+                      (int64_t)js[m] * p.st.kn;
+        const T* vr = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb +
+                      (int64_t)js[m] * p.st.vn;
+        kv[m] = load_cols4<T>(kr, sub * 4, p.d, vec);
+        vv[m] = load_cols4<T>(vr, sub * 4, p.d, vec);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < G; ++m)
+      if (m < cnt) apply(p, kv[m], vv[m]);
+  }
+
+  // one online-softmax step with a loaded K and V piece
+  __device__ __forceinline__ void apply(const AttnParams& p, const float4 kv,
+                                        const float4 vv) {
     float s = q.x * kv.x;
     s = fmaf(q.y, kv.y, s);
     s = fmaf(q.z, kv.z, s);
@@ -81,9 +114,216 @@ struct PrescoreRow {
     T* orow = static_cast<T*>(p.o) + (int64_t)b * p.st.ob + (int64_t)i * p.st.on;
     float o[4] = {acc.x / den, acc.y / den, acc.z / den, acc.w / den};
     if (bad) o[0] = o[1] = o[2] = o[3] = __int_as_float(0x7fc00000);
+    if (p.vec != 0) {  // c + 4 <= d and the piece is 16-byte (8-byte) aligned
+      if constexpr (sizeof(T) == 4) {
+        *reinterpret_cast<float4*>(orow + c) = make_float4(o[0], o[1], o[2], o[3]);
+      } else {
+        const __nv_bfloat162 lo = __floats2bfloat162_rn(o[0], o[1]);
+        const __nv_bfloat162 hi = __floats2bfloat162_rn(o[2], o[3]);
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t*>(&lo);
+        u.y = *reinterpret_cast<const uint32_t*>(&hi);
+        *reinterpret_cast<uint2*>(orow + c) = u;
+      }
+      return;
+    }
 #pragma unroll
     for (int e = 0; e < 4; ++e)
       if (c + e < p.d) orow[c + e] = from_f32<T>(o[e]);
+  }
+};
+
+// One query row per thread, d <= DT (DT = 8 or 16): the whole row's
+// softmax runs once (no lanes repeating it, no shuffles), peers are taken
+// two at a time with all their K and V pieces loaded before the first
+// score. The dot product adds the four 4-column partial sums as
+// (s0 + s2) + (s1 + s3), the order the lane-split form produces.
+template <int DT, typename T>
+struct PrescoreRowThread {
+  float q[DT], acc[DT];
+  float run_max, den;
+
+  __device__ __forceinline__ static void load_row(float (&x)[DT], const T* r,
+                                                  int d, bool vec) {
+#pragma unroll
+    for (int c = 0; c < DT; c += 4) {
+      const float4 f = load_cols4<T>(r, c, d, vec);
+      x[c] = f.x; x[c + 1] = f.y; x[c + 2] = f.z; x[c + 3] = f.w;
+    }
+  }
+
+  __device__ __forceinline__ void init(const AttnParams& p, const T* qr,
+                                       bool live) {
+#pragma unroll
+    for (int c = 0; c < DT; ++c) { q[c] = 0.f; acc[c] = 0.f; }
+    if (live) {
+      load_row(q, qr, p.d, p.vec != 0);
+#pragma unroll
+      for (int c = 0; c < DT; ++c) q[c] *= p.qscale;
+    }
+    run_max = -INFINITY;
+    den = 0.f;
+  }
+
+  // peers kr[0..cnt), vr[0..cnt) (cnt <= 2), rows already range-checked
+  __device__ __forceinline__ void steps2(const AttnParams& p,
+                                         const T* const (&kr)[2],
+                                         const T* const (&vr)[2], int cnt) {
+    const bool vec = p.vec != 0;
+    float kx[2][DT], vx[2][DT];
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+      if (m < cnt) {
+        load_row(kx[m], kr[m], p.d, vec);
+        load_row(vx[m], vr[m], p.d, vec);
+      }
+    apply2(p, kx, vx, cnt);
+  }
+
+  // The same with the peer rows js[0..cnt) read from shared memory: K rows
+  // at sK, V rows at sV, 16-byte piece c of row j at byte off(j, c) (pieces
+  // beyond d hold zeros).
+  template <typename Off>
+  __device__ __forceinline__ void steps2_shared(const AttnParams& p,
+                                                uint32_t sK, uint32_t sV,
+                                                const int (&js)[2], int cnt,
+                                                Off off) {
+    constexpr int EP = 16 / (int)sizeof(T);
+    float kx[2][DT], vx[2][DT];
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+      if (m < cnt) {
+#pragma unroll
+        for (int c = 0; c < DT / EP; ++c) {
+          const uint32_t o = off(js[m], c);
+          load_piece(kx[m], c * EP, sK + o);
+          load_piece(vx[m], c * EP, sV + o);
+        }
+      }
+    apply2(p, kx, vx, cnt);
+  }
+
+  // One peer row j from shared memory (K rows at sK, V rows at sV, piece c
+  // of row j at byte off(j, c), zeros beyond d): the score from K pieces,
+  // then the accumulator from V pieces, so only one piece is held at a
+  // time. Same arithmetic as apply2.
+  template <typename Off>
+  __device__ __forceinline__ void step_shared(const AttnParams& p, uint32_t sK,
+                                              uint32_t sV, int j, Off off) {
+    constexpr int EP = 16 / (int)sizeof(T);
+    float part[DT / 4];
+#pragma unroll
+    for (int c = 0; c < DT / EP; ++c) {
+      float x[DT];
+      load_piece(x, c * EP, sK + off(j, c));
+#pragma unroll
+      for (int g = c * EP / 4; g < (c + 1) * EP / 4; ++g) {
+        float t = q[4 * g] * x[4 * g];
+        t = fmaf(q[4 * g + 1], x[4 * g + 1], t);
+        t = fmaf(q[4 * g + 2], x[4 * g + 2], t);
+        part[g] = fmaf(q[4 * g + 3], x[4 * g + 3], t);
+      }
+    }
+    float s;
+    if constexpr (DT == 16)
+      s = (part[0] + part[2]) + (part[1] + part[3]);
+    else
+      s = part[0] + part[1];
+    s *= p.post_scale;
+    const float m_new = fmaxf(run_max, s);
+    const float alpha = (run_max == -INFINITY) ? 0.f : expf(run_max - m_new);
+    const float pe = expf(s - m_new);
+    den = den * alpha + pe;
+#pragma unroll
+    for (int c = 0; c < DT / EP; ++c) {
+      float x[DT];
+      load_piece(x, c * EP, sV + off(j, c));
+#pragma unroll
+      for (int e = c * EP; e < (c + 1) * EP; ++e)
+        acc[e] = acc[e] * alpha + pe * x[e];
+    }
+    run_max = m_new;
+  }
+
+  // 16 bytes of shared memory -> EP values at x[c0..c0+EP)
+  __device__ __forceinline__ static void load_piece(float (&x)[DT], int c0,
+                                                    uint32_t addr) {
+    uint32_t u[4];
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(u[0]), "=r"(u[1]), "=r"(u[2]), "=r"(u[3])
+                 : "r"(addr));
+    if constexpr (sizeof(T) == 4) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) x[c0 + e] = __uint_as_float(u[e]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 f = __bfloat1622float2(
+            *reinterpret_cast<const __nv_bfloat162*>(&u[e]));
+        x[c0 + 2 * e] = f.x;
+        x[c0 + 2 * e + 1] = f.y;
+      }
+    }
+  }
+
+  __device__ __forceinline__ void apply2(const AttnParams& p,
+                                         const float (&kx)[2][DT],
+                                         const float (&vx)[2][DT], int cnt) {
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+      if (m < cnt) {
+        float part[DT / 4];
+#pragma unroll
+        for (int g = 0; g < DT / 4; ++g) {
+          float t = q[4 * g] * kx[m][4 * g];
+          t = fmaf(q[4 * g + 1], kx[m][4 * g + 1], t);
+          t = fmaf(q[4 * g + 2], kx[m][4 * g + 2], t);
+          part[g] = fmaf(q[4 * g + 3], kx[m][4 * g + 3], t);
+        }
+        float s;
+        if constexpr (DT == 16)
+          s = (part[0] + part[2]) + (part[1] + part[3]);
+        else
+          s = part[0] + part[1];
+        s *= p.post_scale;
+        const float m_new = fmaxf(run_max, s);
+        const float alpha = (run_max == -INFINITY) ? 0.f : expf(run_max - m_new);
+        const float pe = expf(s - m_new);
+        den = den * alpha + pe;
+#pragma unroll
+        for (int c = 0; c < DT; ++c) acc[c] = acc[c] * alpha + pe * vx[m][c];
+        run_max = m_new;
+      }
+  }
+
+  __device__ __forceinline__ void finish(const AttnParams& p, T* orow,
+                                         bool bad) {
+    float o[DT];
+#pragma unroll
+    for (int c = 0; c < DT; ++c)
+      o[c] = bad ? __int_as_float(0x7fc00000) : acc[c] / den;
+    if (p.vec != 0) {  // d % 4 == 0, 16-byte (8-byte) aligned rows
+#pragma unroll
+      for (int c = 0; c < DT; c += 4) {
+        if (c < p.d) {
+          if constexpr (sizeof(T) == 4) {
+            *reinterpret_cast<float4*>(orow + c) =
+                make_float4(o[c], o[c + 1], o[c + 2], o[c + 3]);
+          } else {
+            const __nv_bfloat162 lo = __floats2bfloat162_rn(o[c], o[c + 1]);
+            const __nv_bfloat162 hi = __floats2bfloat162_rn(o[c + 2], o[c + 3]);
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t*>(&lo);
+            u.y = *reinterpret_cast<const uint32_t*>(&hi);
+            *reinterpret_cast<uint2*>(orow + c) = u;
+          }
+        }
+      }
+      return;
+    }
+#pragma unroll
+    for (int c = 0; c < DT; ++c)
+      if (c < p.d) orow[c] = from_f32<T>(o[c]);
   }
 };
 
