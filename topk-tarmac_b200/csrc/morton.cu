@@ -590,20 +590,12 @@ __global__ void __launch_bounds__(MW_THREADS) morton_prescore_regs_kernel(
 // over all 8 bank groups. Dynamic shared memory: K then V, N rows of DT
 // elements each. The block has one thread per query row (up to 512); the
 // sort runs on its first four warps.
-template <int DT, typename T>
-__device__ __forceinline__ uint32_t kv_piece_off(int row, int c) {
-  constexpr int CPR = DT * (int)sizeof(T) / 16;  // 16-byte pieces per row
-  const int sw = CPR == 4 ? ((row >> 1) & 3) : (CPR == 2 ? ((row >> 2) & 1) : 0);
-  return (uint32_t)(row * CPR + (c ^ sw)) * 16u;
-}
-
 template <int WS, int P, int DT, typename T, int NT>
 __global__ void __launch_bounds__(NT) morton_prescore_smem_kernel(
     AttnParams p, const float* __restrict__ pos, int bits,
     int64_t* __restrict__ idx_out) {
   constexpr int M = WS * 32 * P;
   constexpr int CPR = DT * (int)sizeof(T) / 16;
-  constexpr int EP = 16 / (int)sizeof(T);  // elements per piece
   __shared__ unsigned long long sk[M];
   __shared__ int ord[M];
   __shared__ int rank[M];
@@ -613,24 +605,11 @@ __global__ void __launch_bounds__(NT) morton_prescore_smem_kernel(
   __shared__ int wsum[2 * MW_WARPS];
   __shared__ float red[4 * MW_WARPS];
   extern __shared__ __align__(16) unsigned char kv_smem[];
-  const int N = p.N, k = p.topk, d = p.d;
+  const int N = p.N, k = p.topk;
   const int b = blockIdx.x;
-  const T* Kb = static_cast<const T*>(p.k) + (int64_t)b * p.st.kb;
-  const T* Vb = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
   const uint32_t sK = tc_smem_base(kv_smem);
   const uint32_t sV = sK + (uint32_t)N * CPR * 16u;
-  for (int e = threadIdx.x; e < N * CPR; e += NT) {
-    const int r = e / CPR, c = e - r * CPR;
-    const uint32_t off = kv_piece_off<DT, T>(r, c);
-    if (c * EP < d) {
-      cp_async16_addr(sK + off, Kb + (int64_t)r * p.st.kn + c * EP);
-      cp_async16_addr(sV + off, Vb + (int64_t)r * p.st.vn + c * EP);
-    } else {
-      st_shared_zero16(sK + off);
-      st_shared_zero16(sV + off);
-    }
-  }
-  cp_async_commit();
+  stage_kv_episode<DT, T, NT>(p, b, sK, sV);
   morton_order_episode<WS, P>(pos + (int64_t)b * N * 2, N, bits, ord, rank, sk,
                               red, code, bst, memb, wsum);
   cp_async_wait<0>();
@@ -717,18 +696,6 @@ static cudaError_t launch_mps(const AttnParams& p, const float* pos, int bits,
   morton_prescore_smem_kernel<WS, P, DT, T, NT><<<p.B, NT, sm, s>>>(
       p, pos, bits, idx_out);
   return cudaGetLastError();
-}
-
-// K and V rows can be staged in shared memory by whole 16-byte pieces
-template <typename T>
-static bool kv_stageable(const AttnParams& p) {
-  constexpr int EP = 16 / (int)sizeof(T);
-  const auto a16 = [](const void* x) {
-    return reinterpret_cast<uintptr_t>(x) % 16 == 0;
-  };
-  return p.vec != 0 && p.d % EP == 0 && a16(p.k) && a16(p.v) &&
-         p.st.kb % EP == 0 && p.st.kn % EP == 0 && p.st.vb % EP == 0 &&
-         p.st.vn % EP == 0;
 }
 
 template <int DP, typename T>

@@ -327,4 +327,55 @@ struct PrescoreRowThread {
   }
 };
 
+// ---------------------------------------------------------------------------
+// One episode's K and V rows in shared memory (d <= DT <= 16, 16-byte rows)
+// ---------------------------------------------------------------------------
+// Byte offset of 16-byte piece c of row `row`: the pieces of a row are
+// XOR-swizzled by bits of the row index, so the pieces a warp gathers from
+// 32 random rows spread over all 8 bank groups (64-byte fp32 rows: bits 1-2;
+// 32-byte bf16 rows: bit 2).
+template <int DT, typename T>
+__device__ __forceinline__ uint32_t kv_piece_off(int row, int c) {
+  constexpr int CPR = DT * (int)sizeof(T) / 16;  // 16-byte pieces per row
+  const int sw = CPR == 4 ? ((row >> 1) & 3) : (CPR == 2 ? ((row >> 2) & 1) : 0);
+  return (uint32_t)(row * CPR + (c ^ sw)) * 16u;
+}
+
+// Start 16-byte cp.async copies of episode b's N K rows to sK and V rows to
+// sV (shared-window addresses, N * DT * sizeof(T) bytes each); pieces beyond
+// d are zero-filled. NT threads; the caller waits (cp_async_wait<0>) and
+// synchronises the block before reading.
+template <int DT, typename T, int NT>
+__device__ __forceinline__ void stage_kv_episode(const AttnParams& p, int b,
+                                                 uint32_t sK, uint32_t sV) {
+  constexpr int CPR = DT * (int)sizeof(T) / 16;
+  constexpr int EP = 16 / (int)sizeof(T);
+  const T* Kb = static_cast<const T*>(p.k) + (int64_t)b * p.st.kb;
+  const T* Vb = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
+  for (int e = threadIdx.x; e < p.N * CPR; e += NT) {
+    const int r = e / CPR, c = e - r * CPR;
+    const uint32_t off = kv_piece_off<DT, T>(r, c);
+    if (c * EP < p.d) {
+      cp_async16_addr(sK + off, Kb + (int64_t)r * p.st.kn + c * EP);
+      cp_async16_addr(sV + off, Vb + (int64_t)r * p.st.vn + c * EP);
+    } else {
+      st_shared_zero16(sK + off);
+      st_shared_zero16(sV + off);
+    }
+  }
+  cp_async_commit();
+}
+
+// K and V rows can be staged by whole 16-byte pieces with cp.async
+template <typename T>
+inline bool kv_stageable(const AttnParams& p) {
+  constexpr int EP = 16 / (int)sizeof(T);
+  const auto a16 = [](const void* x) {
+    return reinterpret_cast<uintptr_t>(x) % 16 == 0;
+  };
+  return p.vec != 0 && p.d % EP == 0 && a16(p.k) && a16(p.v) &&
+         p.st.kb % EP == 0 && p.st.kn % EP == 0 && p.st.vb % EP == 0 &&
+         p.st.vn % EP == 0;
+}
+
 }  // namespace tarmac
