@@ -484,19 +484,39 @@ __device__ __forceinline__ void morton_order_episode(
   __syncthreads();
 }
 
+// Shared scratch of the register-tier sort kernels. The bitonic keys (only
+// used when an episode falls back to the bitonic network, after the bucket
+// arrays are dead) share their space with the codes and bucket starts.
+template <int M>
+struct SortScratch {
+  union {
+    unsigned long long sk[M];
+    struct {
+      uint32_t code[M];
+      int bst[M];
+    } b;
+  } u;
+  int ord[M];
+  int rank[M];
+  int memb[M];
+  int wsum[2 * MW_WARPS];
+  float red[4 * MW_WARPS];
+};
+
 template <int WS, int P>
 __global__ void __launch_bounds__(MW_THREADS) morton_select_regs_kernel(
     const float* __restrict__ pos, int N, int k, int bits,
     int64_t* __restrict__ idx_out) {
   constexpr int M = WS * 32 * P;
-  __shared__ unsigned long long sk[M];
-  __shared__ int ord[M];
-  __shared__ int rank[M];
-  __shared__ uint32_t code[M];
-  __shared__ int bst[M];
-  __shared__ int memb[M];
-  __shared__ int wsum[2 * MW_WARPS];
-  __shared__ float red[4 * MW_WARPS];
+  __shared__ SortScratch<M> S;
+  unsigned long long* sk = S.u.sk;
+  int* ord = S.ord;
+  int* rank = S.rank;
+  uint32_t* code = S.u.b.code;
+  int* bst = S.u.b.bst;
+  int* memb = S.memb;
+  int* wsum = S.wsum;
+  float* red = S.red;
   const int b = blockIdx.x;
   morton_order_episode<WS, P>(pos + (int64_t)b * N * 2, N, bits, ord, rank, sk,
                               red, code, bst, memb, wsum);
@@ -512,14 +532,15 @@ __global__ void __launch_bounds__(MW_THREADS) morton_prescore_regs_kernel(
     AttnParams p, const float* __restrict__ pos, int bits,
     int64_t* __restrict__ idx_out) {
   constexpr int M = WS * 32 * P;
-  __shared__ unsigned long long sk[M];
-  __shared__ int ord[M];
-  __shared__ int rank[M];
-  __shared__ uint32_t code[M];
-  __shared__ int bst[M];
-  __shared__ int memb[M];
-  __shared__ int wsum[2 * MW_WARPS];
-  __shared__ float red[4 * MW_WARPS];
+  __shared__ SortScratch<M> S;
+  unsigned long long* sk = S.u.sk;
+  int* ord = S.ord;
+  int* rank = S.rank;
+  uint32_t* code = S.u.b.code;
+  int* bst = S.u.b.bst;
+  int* memb = S.memb;
+  int* wsum = S.wsum;
+  float* red = S.red;
   const int N = p.N, k = p.topk;
   const int b = blockIdx.x;
   morton_order_episode<WS, P>(pos + (int64_t)b * N * 2, N, bits, ord, rank, sk,
@@ -588,22 +609,23 @@ __global__ void __launch_bounds__(MW_THREADS) morton_prescore_regs_kernel(
 // conflicts. A row's 16-byte pieces are stored XOR-swizzled by bits 1-2 of
 // the row index, so the pieces a warp gathers from 32 random rows spread
 // over all 8 bank groups. Dynamic shared memory: K then V, N rows of DT
-// elements each. The block has one thread per query row (up to 512); the
-// sort runs on its first four warps.
+// elements each. The block has up to 256 threads, one or two query rows per
+// thread; the sort runs on its first four warps.
 template <int WS, int P, int DT, typename T, int NT>
 __global__ void __launch_bounds__(NT) morton_prescore_smem_kernel(
     AttnParams p, const float* __restrict__ pos, int bits,
     int64_t* __restrict__ idx_out) {
   constexpr int M = WS * 32 * P;
   constexpr int CPR = DT * (int)sizeof(T) / 16;
-  __shared__ unsigned long long sk[M];
-  __shared__ int ord[M];
-  __shared__ int rank[M];
-  __shared__ uint32_t code[M];
-  __shared__ int bst[M];
-  __shared__ int memb[M];
-  __shared__ int wsum[2 * MW_WARPS];
-  __shared__ float red[4 * MW_WARPS];
+  __shared__ SortScratch<M> S;
+  unsigned long long* sk = S.u.sk;
+  int* ord = S.ord;
+  int* rank = S.rank;
+  uint32_t* code = S.u.b.code;
+  int* bst = S.u.b.bst;
+  int* memb = S.memb;
+  int* wsum = S.wsum;
+  float* red = S.red;
   extern __shared__ __align__(16) unsigned char kv_smem[];
   const int N = p.N, k = p.topk;
   const int b = blockIdx.x;
@@ -682,12 +704,14 @@ static cudaError_t launch_mpr(const AttnParams& p, const float* pos, int bits,
   return cudaGetLastError();
 }
 
-// one query row per thread: NT = the sort's key count M, at least 128
+// NT = half the sort's key count, at least 128 threads (one or two query
+// rows per thread): with the 64 KB of K and V at N = 512, three blocks fit
+// an SM, so one block's sort runs beside another's attention rows
 template <int WS, int P, int DT, typename T>
 static cudaError_t launch_mps(const AttnParams& p, const float* pos, int bits,
                               int64_t* idx_out, cudaStream_t s) {
   constexpr int M = WS * 32 * P;
-  constexpr int NT = M < MW_THREADS ? MW_THREADS : M;
+  constexpr int NT = M / 2 < MW_THREADS ? MW_THREADS : M / 2;
   const size_t sm = (size_t)2 * p.N * DT * sizeof(T);
   cudaError_t e = cudaFuncSetAttribute(
       morton_prescore_smem_kernel<WS, P, DT, T, NT>,
