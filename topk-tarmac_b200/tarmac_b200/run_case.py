@@ -23,7 +23,8 @@ def main() -> int:
                                  formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--op", default="topk",
                     choices=("topk", "topk_sort", "topk_threshold", "stream",
-                             "dense", "morton_prescore", "morton_select"))
+                             "dense", "morton_prescore", "morton_select",
+                             "prescore"))
     ap.add_argument("--B", type=int, default=1024)
     ap.add_argument("--N", type=int, default=512)
     ap.add_argument("--d", type=int, default=16)
@@ -43,6 +44,8 @@ def main() -> int:
     q, k, v = (torch.randn(a.B, a.N, a.d, generator=g).to(dt).cuda()
                for _ in range(3))
     pos = torch.rand(a.B, a.N, 2, generator=g).cuda()
+    # the Z-order window indices, for the stand-alone prescore op
+    widx = ops.morton_select(pos, a.k, bits=a.bits) if a.op == "prescore" else None
     calls = {
         "topk": lambda: ops.topk_attention(q, k, v, a.k),
         "topk_sort": lambda: ops.topk_attention(q, k, v, a.k, mode="sort"),
@@ -53,6 +56,7 @@ def main() -> int:
         "morton_prescore": lambda: ops.morton_prescore_attention(
             q, k, v, pos, a.k, bits=a.bits),
         "morton_select": lambda: ops.morton_select(pos, a.k, bits=a.bits),
+        "prescore": lambda: ops.prescore_attention(q, k, v, widx),
     }
     fn = calls[a.op]
     fn()
