@@ -188,12 +188,17 @@ static cudaError_t launch_dense_dt(const AttnParams& p, cudaStream_t s) {
 
 bool dense_tc_supported(const AttnParams& p);
 cudaError_t launch_dense_tc(const AttnParams& p, cudaStream_t s);
+bool dense_tc_f32_supported(const AttnParams& p);
+cudaError_t launch_dense_tc_f32(const AttnParams& p, cudaStream_t s);
 
-// bf16 episodes of 128 or more agents run on the tensor cores (dense_tc.cu);
-// fp32 inputs and small bf16 episodes on the packed-FMA kernel above.
+// Episodes of 128 or more agents run on the tensor cores (dense_tc.cu): bf16
+// directly, fp32 with d in {8, 16} and 16-byte rows as three exact bf16
+// planes; other shapes on the packed-FMA kernel above.
 cudaError_t launch_dense(const AttnParams& p, int dtype, cudaStream_t s) {
   if (dtype == TARMAC_BF16 && dense_tc_supported(p))
     return launch_dense_tc(p, s);
+  if (dtype == TARMAC_F32 && dense_tc_f32_supported(p))
+    return launch_dense_tc_f32(p, s);
   return dtype == TARMAC_BF16 ? launch_dense_dt<__nv_bfloat16>(p, s)
                               : launch_dense_dt<float>(p, s);
 }

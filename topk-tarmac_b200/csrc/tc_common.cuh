@@ -446,13 +446,16 @@ __device__ __forceinline__ void split3_bf16x2(float a, float b, uint32_t& hi,
 
 // A tile of R fp32 rows (DP columns, zero beyond d and beyond the first
 // `nvalid` rows) held in registers between a global load and a split store
-// into three bf16 K-major core-matrix planes (hi, mid, lo) of `plane` bytes
-// each. 128 threads; item e = threadIdx.x + 128 u is the 8-element piece
-// (row ((e / 8) / KCH) * 8 + e % 8, chunk (e / 8) % KCH) whose bf16 image
-// sits at byte 16 e of each plane, so the 8 lanes of a shared-memory
-// wavefront write 128 contiguous bytes and a warp reads 16 whole rows.
+// into three bf16 core-matrix planes (hi, mid, lo) of `plane` bytes each.
+// 128 threads; item e = threadIdx.x + 128 u is the 8-element piece
+// (row r = ((e / 8) / KCH) * 8 + e % 8, chunk c = (e / 8) % KCH). K-major
+// planes (MN = false): the piece's bf16 image sits at byte 16 e, so the 8
+// lanes of a shared-memory wavefront write 128 contiguous bytes and a warp
+// reads 16 whole rows. MN-major planes (MN = true, the rows being the
+// contraction dimension, as V in P.V): the piece sits at byte
+// ((r / 8) + c * (R / 8)) * 128 + (r % 8) * 16, the MN-major layout above.
 // Requires d % 8 == 0 and 16-byte aligned rows (row stride % 4 == 0).
-template <int DP, int R>
+template <int DP, int R, bool MN = false>
 struct SplitTile {
   static constexpr int KCH = DP / 8;
   static constexpr int U = R * KCH / 128;
@@ -481,7 +484,14 @@ struct SplitTile {
   __device__ __forceinline__ void store(uint32_t base, uint32_t plane) const {
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const uint32_t dst = base + (uint32_t)(threadIdx.x + 128 * u) * 16u;
+      const int e = threadIdx.x + 128 * u;
+      uint32_t off = (uint32_t)e * 16u;
+      if constexpr (MN) {
+        const int r = ((e >> 3) / KCH) * 8 + (e & 7);
+        const int c = (e >> 3) % KCH;
+        off = (uint32_t)(((r >> 3) + c * (R / 8)) * 128 + (r & 7) * 16);
+      }
+      const uint32_t dst = base + off;
       uint32_t h[4], m[4], l[4];
       split3_bf16x2(x[u][0].x, x[u][0].y, h[0], m[0], l[0]);
       split3_bf16x2(x[u][0].z, x[u][0].w, h[1], m[1], l[1]);
