@@ -26,12 +26,12 @@
  * scores on the tensor cores (exact bf16 products, fp32 accumulation; the
  * dense path feeds its softmax weights to P.V as bf16, as the reference's
  * bf16 kernel does); other bf16 inputs are widened to fp32 on load. fp32
- * top-k inputs with N >= 128, d a multiple of 8 up to 16, k <= 8 and 16-byte
- * aligned rows also form their scores on the tensor cores: each q and k is
- * split exactly into three bf16 parts and six part products accumulate in
- * fp32, an fp32-accurate dot product (error within about
- * 2^-23 * sum_c |q_c k_c| plus fp32 accumulation rounding). Other fp32 work
- * uses IEEE fp32 FMA.
+ * top-k (k <= 8) and dense inputs with N >= 128, d a multiple of 8 up to 16
+ * and 16-byte aligned rows also run on the tensor cores: every operand (q,
+ * k, v and the dense path's softmax weights) is split exactly into three
+ * bf16 parts and six part products accumulate in fp32, an fp32-accurate
+ * product (error within about 2^-23 * sum_c |a_c b_c| plus fp32
+ * accumulation rounding). Other fp32 work uses IEEE fp32 FMA.
  *
  * Row-count and width limits: 2 <= N, 1 <= d <= 128; `scale` must be positive
  * and finite (TARMAC_ERR_SHAPE otherwise).
