@@ -72,26 +72,28 @@ __host__ __device__ constexpr int tc_chunk(int KC, bool f32) {
              : (KC <= 2 ? 32 : (KC == 4 ? 16 : 8));
 }
 
-// Insert chunk (cm, cid) into the descending list (mv, mc, ms) of KC chunks
-// under the streaming tie rule; the dropped last entry's slot goes to the
-// new chunk.
+// A chunk-list entry packs the chunk id and the shared-memory slot holding
+// its saved scores as (id << 3) | slot; an empty entry has id -1, so it is
+// negative and sorts last as an unsigned value.
+__device__ __forceinline__ int entry_id(int e) { return e >> 3; }
+__device__ __forceinline__ int entry_slot(int e) { return e & 7; }
+
+// Insert chunk maximum cm with entry ce into the descending list (mv, me) of
+// KC chunks under the streaming tie rule, branch-free; a chunk that does not
+// beat the last entry leaves the list unchanged.
 template <int KC, bool TIE_HIGH>
-__device__ __forceinline__ void chunk_insert(float (&mv)[KC], int (&mc)[KC],
-                                             int (&ms)[KC], float cm, int cid,
-                                             int slot) {
+__device__ __forceinline__ void chunk_insert(float (&mv)[KC], int (&me)[KC],
+                                             float cm, int ce) {
 #pragma unroll
   for (int p = KC - 1; p >= 1; --p) {
     const bool here = beats<TIE_HIGH>(cm, mv[p]);
     const bool above = beats<TIE_HIGH>(cm, mv[p - 1]);
     mv[p] = above ? mv[p - 1] : (here ? cm : mv[p]);
-    mc[p] = above ? mc[p - 1] : (here ? cid : mc[p]);
-    ms[p] = above ? ms[p - 1] : (here ? slot : ms[p]);
+    me[p] = above ? me[p - 1] : (here ? ce : me[p]);
   }
-  if (beats<TIE_HIGH>(cm, mv[0])) {
-    mv[0] = cm;
-    mc[0] = cid;
-    ms[0] = slot;
-  }
+  const bool top = beats<TIE_HIGH>(cm, mv[0]);
+  mv[0] = top ? cm : mv[0];
+  me[0] = top ? ce : me[0];
 }
 
 template <typename T, int DP, int KC, bool TIE_HIGH>
@@ -179,12 +181,11 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
 
   // chunk list; padding rows (i >= N) start full of +inf and admit nothing
   float mv[KC];
-  int mc[KC], ms[KC];
+  int me[KC];
 #pragma unroll
   for (int m = 0; m < KC; ++m) {
     mv[m] = i < N ? -INFINITY : INFINITY;
-    mc[m] = -1;
-    ms[m] = m;
+    me[m] = (-1 * 8) | m;  // empty, slot m
   }
   float4* my_slots = sv + row * (RG + 1);
 
@@ -273,19 +274,21 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
         for (int t = 1; t + 1 < CH; t += 2)
           cm = max3f(cm, v[u * CH + t], v[u * CH + t + 1]);
         cm = fmaxf(cm, v[u * CH + CH - 1]);
+        // A chunk entering the list takes the slot of the entry it evicts.
+        // Almost every chunk admits some lane of the warp, so the list
+        // update runs for every chunk without a vote or a branch; only the
+        // saved-score stores are conditional.
         const bool enter = beats<TIE_HIGH>(cm, mv[KC - 1]);
-        if (__any_sync(0xffffffffu, enter)) {
-          if (enter) {
-            const int slot = ms[KC - 1];
-            float4* dst = my_slots + slot * G;
+        const int slot = entry_slot(me[KC - 1]);
+        if (enter) {
+          float4* dst = my_slots + slot * G;
 #pragma unroll
-            for (int g = 0; g < G; ++g)
-              dst[g] = make_float4(v[u * CH + 4 * g], v[u * CH + 4 * g + 1],
-                                   v[u * CH + 4 * g + 2], v[u * CH + 4 * g + 3]);
-            chunk_insert<KC, TIE_HIGH>(mv, mc, ms, cm, (j0 + u * CH) / CH,
-                                       slot);
-          }
+          for (int g = 0; g < G; ++g)
+            dst[g] = make_float4(v[u * CH + 4 * g], v[u * CH + 4 * g + 1],
+                                 v[u * CH + 4 * g + 2], v[u * CH + 4 * g + 3]);
         }
+        chunk_insert<KC, TIE_HIGH>(mv, me, cm,
+                                   (((j0 + u * CH) / CH) << 3) | slot);
       }
     }
     if constexpr (F32) {
@@ -300,18 +303,16 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
   // ---- pass 2: exact k best among the saved chunks ------------------------
   // The saved chunks, visited in increasing key order, are a stream holding
   // the k best scores of the row; the streaming insert keeps them under the
-  // tie rule. Empty entries (mc < 0) sort last and are skipped.
+  // tie rule. Entries sort by chunk id (their high bits); empty entries
+  // (negative) sort last as unsigned values and are skipped.
 #pragma unroll
   for (int a = 0; a < KC; ++a)
 #pragma unroll
     for (int m = 0; m + 1 < KC - a; ++m) {
-      const unsigned x = (unsigned)mc[m], y = (unsigned)mc[m + 1];
+      const unsigned x = (unsigned)me[m], y = (unsigned)me[m + 1];
       const bool sw = x > y;
-      mc[m] = sw ? (int)y : (int)x;
-      mc[m + 1] = sw ? (int)x : (int)y;
-      const int t = ms[m];
-      ms[m] = sw ? ms[m + 1] : t;
-      ms[m + 1] = sw ? t : ms[m + 1];
+      me[m] = sw ? (int)y : (int)x;
+      me[m + 1] = sw ? (int)x : (int)y;
     }
   float bs[KC];
   int bi[KC];
@@ -322,9 +323,9 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
   }
 #pragma unroll
   for (int m = 0; m < KC; ++m) {
-    if (mc[m] < 0) break;
-    const int jb = mc[m] * CH;
-    const float4* src = my_slots + ms[m] * G;
+    if (me[m] < 0) break;
+    const int jb = entry_id(me[m]) * CH;
+    const float4* src = my_slots + entry_slot(me[m]) * G;
 #pragma unroll
     for (int g = 0; g < G; ++g) {
       const float4 f = src[g];
