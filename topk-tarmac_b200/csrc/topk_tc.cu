@@ -63,14 +63,14 @@ __host__ __device__ constexpr int tc_bufs(int DP) { return DP <= 16 ? 1 : 2; }
 // bf16 planes per operand: one, or hi / mid / lo for fp32
 __host__ __device__ constexpr int tc_planes(bool f32) { return f32 ? 3 : 1; }
 
-// keys per chunk for a list of KC chunks: 32 for KC = 1, 16 for KC = 2 (and
-// for bf16 KC = 4), else 8. Shorter chunks cost more list updates but make
-// pass 2 and the saved-score slots smaller (32 floats per row up to KC = 4,
-// 64 at KC = 8), which keeps the fp32 operand planes within four blocks per
-// SM; measured fastest since the list update runs without a warp vote.
+// keys per chunk for a list of KC chunks: 16 for KC <= 2 (bf16: KC <= 4),
+// else 8. Shorter chunks cost more list updates but make pass 2 and the
+// saved-score slots smaller; fp32 at KC = 4 keeps 8-key chunks, since its
+// larger operand planes plus 64 saved floats per row would drop the block
+// to three per SM. Measured fastest once the list update ran without a warp
+// vote.
 __host__ __device__ constexpr int tc_chunk(int KC, bool f32) {
-  return f32 ? (KC == 1 ? 32 : (KC == 2 ? 16 : 8))
-             : (KC == 1 ? 32 : (KC <= 4 ? 16 : 8));
+  return f32 ? (KC <= 2 ? 16 : 8) : (KC <= 4 ? 16 : 8);
 }
 
 // A chunk-list entry packs the chunk id and the shared-memory slot holding
