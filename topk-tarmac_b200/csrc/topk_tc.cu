@@ -63,15 +63,11 @@ __host__ __device__ constexpr int tc_bufs(int DP) { return DP <= 16 ? 1 : 2; }
 // bf16 planes per operand: one, or hi / mid / lo for fp32
 __host__ __device__ constexpr int tc_planes(bool f32) { return f32 ? 3 : 1; }
 
-// keys per chunk for a list of KC chunks: 16 for KC <= 2 (bf16: KC <= 4),
-// else 8. Shorter chunks cost more list updates but make pass 2 and the
-// saved-score slots smaller; fp32 at KC = 4 keeps 8-key chunks, since its
-// larger operand planes plus 64 saved floats per row would drop the block
-// to three per SM. Measured fastest once the list update ran without a warp
-// vote.
-__host__ __device__ constexpr int tc_chunk(int KC, bool f32) {
-  return f32 ? (KC <= 2 ? 16 : 8) : (KC <= 4 ? 16 : 8);
-}
+// keys per chunk: 8 for every list size. Shorter chunks cost more list
+// updates but make pass 2 and the saved-score slots smaller; with the list
+// update branch-free (no warp vote), 8 measured fastest at every k and both
+// dtypes (32, 16 and 4 were slower).
+__host__ __device__ constexpr int tc_chunk(int, bool) { return 8; }
 
 // A chunk-list entry packs the chunk id and the shared-memory slot holding
 // its saved scores as (id << 3) | slot; an empty entry has id -1, so it is
