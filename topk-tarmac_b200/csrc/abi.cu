@@ -5,12 +5,37 @@
 // caller's stream. No memory is allocated and no stream is synchronised.
 #include <math.h>
 
+#include <array>
+#include <mutex>
+#include <unordered_map>
+
 #include "backward.cuh"
 #include "comm.cuh"
 #include "common.cuh"
 #include "topk_chunk.cuh"
 
 namespace tarmac {
+
+cudaError_t raise_smem_limit(const void* fn, size_t bytes) {
+  constexpr int MAX_DEV = 64;
+  static std::mutex mu;
+  static std::unordered_map<const void*, std::array<size_t, MAX_DEV>> done;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find(fn);
+  if (it == done.end()) {
+    std::array<size_t, MAX_DEV> zero{};
+    it = done.emplace(fn, zero).first;
+  }
+  if (dev >= 0 && dev < MAX_DEV && it->second[dev] >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)bytes);
+  if (e == cudaSuccess && dev >= 0 && dev < MAX_DEV) it->second[dev] = bytes;
+  return e;
+}
+
 cudaError_t launch_topk_stream_f32(const AttnParams& p, bool tie_high,
                                    cudaStream_t s);
 cudaError_t launch_topk_stream_bf16(const AttnParams& p, bool tie_high,

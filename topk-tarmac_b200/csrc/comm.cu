@@ -182,9 +182,8 @@ static cudaError_t launch_comm_t(CommParams p, cudaStream_t s) {
   const size_t wb = sizeof(float) * (size_t)3 * p.m * (p.in_dim + 1);
   p.w_smem = sm + wb <= COMM_SMEM_WITH_W;
   if (p.w_smem) sm += wb;
-  cudaError_t e = cudaFuncSetAttribute(comm_forward_kernel<MP, KM>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)comm_forward_kernel<MP, KM>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   comm_forward_kernel<MP, KM><<<p.B, COMM_THREADS, sm, s>>>(p);
   return cudaGetLastError();

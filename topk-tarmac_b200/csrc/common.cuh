@@ -37,6 +37,13 @@ struct AttnParams {
 
 __host__ __device__ constexpr int cdiv(int a, int b) { return (a + b - 1) / b; }
 
+// Raise kernel `fn`'s dynamic shared-memory limit to at least `bytes` on the
+// current device. The attribute lasts for the process, so it is set only
+// when this process has not yet set that much for this kernel and device (a
+// cudaFuncSetAttribute on every launch costs host time that small problems
+// notice). Safe from several host threads (abi.cu).
+cudaError_t raise_smem_limit(const void* fn, size_t bytes);
+
 // ---------------------------------------------------------------------------
 // element conversion
 // ---------------------------------------------------------------------------

@@ -349,9 +349,8 @@ __global__ void __launch_bounds__(DTC_THREADS,
 template <typename T, int DP>
 static cudaError_t launch_dtc(const AttnParams& p, int vec16, cudaStream_t s) {
   const size_t sm = dtc_smem_bytes<DP>(sizeof(T) == 4 ? 3 : 1);
-  cudaError_t e = cudaFuncSetAttribute(
-      dense_tc_kernel<T, DP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-      (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)dense_tc_kernel<T, DP>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   const int64_t blocks = (int64_t)p.B * cdiv(p.N, 128);
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;

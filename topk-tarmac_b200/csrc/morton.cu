@@ -687,9 +687,8 @@ cudaError_t launch_morton_select(const float* pos, int B, int N, int k,
     default: break;
   }
   const size_t sm = sort_smem(N);
-  cudaError_t e = cudaFuncSetAttribute(
-      morton_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-      (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)morton_select_kernel, (size_t)(sm));
   if (e != cudaSuccess) return e;
   morton_select_kernel<<<B, MORTON_THREADS, sm, s>>>(pos, N, next_pow2(N), k,
                                                      bits, idx_out);
@@ -713,9 +712,8 @@ static cudaError_t launch_mps(const AttnParams& p, const float* pos, int bits,
   constexpr int M = WS * 32 * P;
   constexpr int NT = M / 2 < MW_THREADS ? MW_THREADS : M / 2;
   const size_t sm = (size_t)2 * p.N * DT * sizeof(T);
-  cudaError_t e = cudaFuncSetAttribute(
-      morton_prescore_smem_kernel<WS, P, DT, T, NT>,
-      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)morton_prescore_smem_kernel<WS, P, DT, T, NT>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   morton_prescore_smem_kernel<WS, P, DT, T, NT><<<p.B, NT, sm, s>>>(
       p, pos, bits, idx_out);
@@ -747,9 +745,8 @@ static cudaError_t launch_mp_t(const AttnParams& p, const float* pos, int bits,
     default: break;
   }
   const size_t sm = sort_smem(p.N);
-  cudaError_t e = cudaFuncSetAttribute(
-      morton_prescore_kernel<DP, T>,
-      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)morton_prescore_kernel<DP, T>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   morton_prescore_kernel<DP, T><<<p.B, MORTON_THREADS, sm, s>>>(
       p, pos, next_pow2(p.N), bits, idx_out);

@@ -141,9 +141,8 @@ static cudaError_t launch_prescore_episode(const AttnParams& p,
                                            const void* idx, int kk,
                                            cudaStream_t s) {
   const size_t sm = (size_t)2 * p.N * DT * sizeof(T);
-  cudaError_t e = cudaFuncSetAttribute(
-      prescore_episode_kernel<DT, T, I, NT>,
-      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)prescore_episode_kernel<DT, T, I, NT>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   prescore_episode_kernel<DT, T, I, NT><<<p.B, NT, sm, s>>>(
       p, static_cast<const I*>(idx), kk);

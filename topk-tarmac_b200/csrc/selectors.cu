@@ -211,8 +211,8 @@ template <int KM>
 static cudaError_t launch_knn_t(const float* pos, int B, int N, int k,
                                 int64_t* out, cudaStream_t s) {
   const size_t sm = (size_t)N * sizeof(float2);
-  cudaError_t e = cudaFuncSetAttribute(
-      knn_select_kernel<KM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)knn_select_kernel<KM>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   knn_select_kernel<KM><<<B, SEL_THREADS, sm, s>>>(pos, N, k, out);
   return cudaGetLastError();
@@ -223,8 +223,8 @@ static cudaError_t launch_grid_t(const float* pos, int B, int N, int k, int G,
                                  int L, int64_t* out, cudaStream_t s) {
   const int C = G * G;
   const size_t sm = (size_t)N * sizeof(float2) + (size_t)(2 * N + 2 * C + 1) * 4;
-  cudaError_t e = cudaFuncSetAttribute(
-      grid_knn_kernel<KM>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)grid_knn_kernel<KM>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   grid_knn_kernel<KM><<<B, SEL_THREADS, sm, s>>>(pos, N, k, G, L, out);
   return cudaGetLastError();

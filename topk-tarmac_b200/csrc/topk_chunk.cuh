@@ -367,9 +367,8 @@ cudaError_t launch_chunk_t(const AttnParams& p, cudaStream_t s) {
   constexpr int CH = chunk_len(KC);
   const int NC = cdiv(p.N, CH);
   const size_t sm = chunk_smem_bytes<DP, QPT, KC, CH>(NC);
-  cudaError_t e = cudaFuncSetAttribute(
-      topk_chunk_kernel<DP, QPT, KC, CH, TIE_HIGH, T>,
-      cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)topk_chunk_kernel<DP, QPT, KC, CH, TIE_HIGH, T>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   const int64_t blocks = (int64_t)p.B * cdiv(p.N, 32 * QPT);
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;

@@ -405,9 +405,8 @@ static cudaError_t launch_tc_t(const AttnParams& p, int flags, cudaStream_t s) {
           (128 + (tc_bufs(DP) + 1) * tc_round(DP)) * DP * 2 +
       (size_t)128 * (KC * tc_chunk(KC, F32) + 4) * 4;
   const size_t sm = need > (size_t)TC_MIN_SMEM ? need : (size_t)TC_MIN_SMEM;
-  cudaError_t e = cudaFuncSetAttribute(topk_tc_kernel<T, DP, KC, TIE_HIGH>,
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sm);
+  cudaError_t e = raise_smem_limit(
+      (const void*)topk_tc_kernel<T, DP, KC, TIE_HIGH>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   const int64_t blocks = (int64_t)p.B * cdiv(p.N, 128);
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;

@@ -127,9 +127,17 @@ def strerror(status: int) -> str:
     return lib().tarmac_strerror(status).decode()
 
 
+_FNS: dict = {}
+
+
 def call(name: str, *args) -> None:
     """Call an entry point and raise :class:`TarmacError` on a non-zero
-    status."""
-    st = getattr(lib(), name)(*args)
+    status. The function objects are looked up once (a per-call attribute
+    lookup on the library costs more than the launch at small sizes)."""
+    fn = _FNS.get(name)
+    if fn is None:
+        fn = getattr(lib(), name)
+        _FNS[name] = fn
+    st = fn(*args)
     if st != OK:
         raise TarmacError(name, st, strerror(st))

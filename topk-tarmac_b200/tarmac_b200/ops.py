@@ -14,6 +14,7 @@ diagonal excluded, softmax over the retained peers, weighted sum of V rows.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 
 import torch
@@ -38,8 +39,29 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
 
+# the raw current-stream handle without building a Stream object (falls back
+# to the public call on a torch without the accessor)
+_RAW_STREAM = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+_SAME_DEVICE = contextlib.nullcontext()
+
+
+def _index(dev: torch.device) -> int:
+    """The device's ordinal (a bare "cuda" device means the current one)."""
+    return torch.cuda.current_device() if dev.index is None else dev.index
+
+
 def _stream(dev: torch.device) -> int:
+    if _RAW_STREAM is not None:
+        return _RAW_STREAM(_index(dev))
     return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _on(dev: torch.device):
+    """Device context for a launch: the library launches on the current
+    device, so switch only when the tensors live on another one."""
+    if dev.index is None or dev.index == torch.cuda.current_device():
+        return _SAME_DEVICE
+    return torch.cuda.device(dev)
 
 
 def _unit_inner(t: torch.Tensor) -> torch.Tensor:
@@ -81,7 +103,7 @@ def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if N < 2:
         return out.fill_(float("nan"))
     strides = _strides(q, k, v, out)  # must outlive the call
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         _lib.call("tarmac_dense_attention", _ptr(q), _ptr(k), _ptr(v),
                   _ptr(out), ctypes.addressof(strides), B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), _stream(q.device))
@@ -107,7 +129,7 @@ def topk_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     idx = (torch.empty((B, N, topk), device=q.device, dtype=torch.int32)
            if return_indices else None)
     strides = _strides(q, k, v, out)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         _lib.call("tarmac_topk_attention", _ptr(q), _ptr(k), _ptr(v),
                   _ptr(out), ctypes.addressof(strides), B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), int(topk), _MODES[mode],
@@ -127,7 +149,7 @@ def streaming_topk_attention(q: torch.Tensor, k: torch.Tensor,
     idx = (torch.empty((B, N, topk), device=q.device, dtype=torch.int32)
            if return_indices else None)
     strides = _strides(q, k, v, out)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         _lib.call("tarmac_streaming_topk_attention", _ptr(q), _ptr(k), _ptr(v),
                   _ptr(out), ctypes.addressof(strides), B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), int(topk), _ptr(idx),
@@ -154,7 +176,7 @@ def prescore_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if kk == 0:
         return out.fill_(float("nan"))
     strides = _strides(q, k, v, out)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         _lib.call("tarmac_prescore_attention", _ptr(q), _ptr(k), _ptr(v),
                   _ptr(out), ctypes.addressof(strides), _ptr(idx),
                   int(idx.dtype == torch.int64), kk, B, N, d,
@@ -177,7 +199,7 @@ def morton_code(pos: torch.Tensor, bits: int = 10) -> torch.Tensor:
     pos = _check_pos(pos)
     B, N, _ = pos.shape
     out = torch.empty((B, N), device=pos.device, dtype=torch.int64)
-    with torch.cuda.device(pos.device):
+    with _on(pos.device):
         _lib.call("tarmac_morton_code", _ptr(pos), B, N, int(bits), _ptr(out),
                   _stream(pos.device))
     return out
@@ -188,7 +210,7 @@ def morton_select(pos: torch.Tensor, k: int, bits: int = 10) -> torch.Tensor:
     pos = _check_pos(pos)
     B, N, _ = pos.shape
     out = torch.empty((B, N, k), device=pos.device, dtype=torch.int64)
-    with torch.cuda.device(pos.device):
+    with _on(pos.device):
         _lib.call("tarmac_morton_select", _ptr(pos), B, N, int(k), int(bits),
                   _ptr(out), _stream(pos.device))
     return out
@@ -208,7 +230,7 @@ def morton_prescore_attention(q: torch.Tensor, k: torch.Tensor,
     idx = (torch.empty((B, N, topk), device=q.device, dtype=torch.int64)
            if return_indices else None)
     strides = _strides(q, k, v, out)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         _lib.call("tarmac_morton_prescore_attention", _ptr(q), _ptr(k),
                   _ptr(v), _ptr(out), ctypes.addressof(strides), _ptr(pos),
                   B, N, d, _DTYPES[q.dtype], _scale(d, scale), int(topk),
@@ -251,7 +273,7 @@ def gather_attention_backward(q: torch.Tensor, k: torch.Tensor,
     dk = torch.empty_like(dq)
     dv = torch.empty_like(dq)
     strides = _strides_n(q, k, v, dout)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         _lib.call("tarmac_gather_attention_backward", _ptr(q), _ptr(k),
                   _ptr(v), _ptr(dout), ctypes.addressof(strides), _ptr(idx),
                   int(idx.dtype == torch.int64), idx.shape[-1], B, N, d,
@@ -279,7 +301,7 @@ def dense_attention_backward(q: torch.Tensor, k: torch.Tensor,
     dv = torch.empty_like(dq)
     work = torch.empty((2, B, N), device=q.device, dtype=torch.float32)
     strides = _strides_n(q, k, v, out, dout)
-    with torch.cuda.device(q.device):
+    with _on(q.device):
         _lib.call("tarmac_dense_attention_backward", _ptr(q), _ptr(k), _ptr(v),
                   _ptr(out), _ptr(dout), ctypes.addressof(strides), B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), _ptr(dq), _ptr(dk),
@@ -301,7 +323,7 @@ def knn_select(pos: torch.Tensor, k: int) -> torch.Tensor:
     pos = _check_pos(pos)
     B, N, _ = pos.shape
     out = torch.empty((B, N, k), device=pos.device, dtype=torch.int64)
-    with torch.cuda.device(pos.device):
+    with _on(pos.device):
         _lib.call("tarmac_knn_select", _ptr(pos), B, N, int(k), _ptr(out),
                   _stream(pos.device))
     return out
@@ -313,7 +335,7 @@ def grid_knn_select(pos: torch.Tensor, k: int) -> torch.Tensor:
     pos = _check_pos(pos)
     B, N, _ = pos.shape
     out = torch.empty((B, N, k), device=pos.device, dtype=torch.int64)
-    with torch.cuda.device(pos.device):
+    with _on(pos.device):
         _lib.call("tarmac_grid_knn_select", _ptr(pos), B, N, int(k),
                   _ptr(out), _stream(pos.device))
     return out
@@ -331,7 +353,7 @@ def random_select(B: int, N: int, k: int, device,
     seed, offset = (int(x) for x in torch.randint(
         0, 2 ** 62, (2,), generator=generator))
     out = torch.empty((B, N, k), device=device, dtype=torch.int64)
-    with torch.cuda.device(device):
+    with _on(device):
         _lib.call("tarmac_random_select", int(B), int(N), int(k), seed,
                   offset, _ptr(out), _stream(device))
     return out
@@ -360,7 +382,7 @@ def comm_forward(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor,
         raise ValueError("weights must be qkv [3m, in_dim], [3m] and proj "
                          "[m, m], [m]")
     out = torch.empty((B, N, m), device=x.device, dtype=torch.float32)
-    with torch.cuda.device(x.device):
+    with _on(x.device):
         _lib.call("tarmac_comm_forward", _ptr(x), _ptr(w_qkv), _ptr(b_qkv),
                   _ptr(w_proj), _ptr(b_proj), B, N, D, m, int(topk),
                   _ptr(out), _stream(x.device))
