@@ -90,3 +90,38 @@ def test_limits_raise_and_module_falls_back():
     with torch.no_grad():
         out, _ = comm(x)                        # layer-by-layer path
     assert out.shape == (2, 2048, 16) and torch.isfinite(out).all()
+
+
+def test_weights_on_another_device_raise():
+    from tarmac_b200 import ops
+    x = torch.randn(4, 6, 16, device="cuda")
+    w = list(_weights(16, 16, 1))                 # left on the CPU
+    with pytest.raises(ValueError):
+        ops.comm_forward(x, *w, 2)
+
+
+@pytest.mark.parametrize("B,N,D,m,topk,offset", [
+    (64, 8, 64, 16, 2, 0),     # N * 16 = 128: the last (agent, column) size
+    (64, 9, 64, 16, 2, 0),     # one agent past it: a thread per agent
+    (64, 16, 20, 8, 3, 0),     # N * 8 = 128 with 16-byte rows of 20 words
+    (64, 6, 64, 16, 2, 1),     # x one word off the 16-byte grid: 4-byte copies
+    (64, 6, 33, 16, 0, 0),     # odd input width: 4-byte copies, dense
+    (32, 4, 64, 32, 2, 0),     # N * 32 = 128
+    (32, 2, 64, 64, 1, 0),     # N * 64 = 128
+    (8, 150, 256, 64, 4, 0)])  # W_qkv left in global memory
+def test_comm_forward_copy_forms_and_phase2_forms(B, N, D, m, topk, offset):
+    """The 16-byte and 4-byte staging forms and both phase-2 forms (one
+    thread per (agent, message column) up to N * padded m = 128, one thread
+    per agent above) against the float64 module oracle."""
+    from tarmac_b200 import ops
+    g = torch.Generator().manual_seed(B + N + D + m)
+    x = torch.randn(B, N, D, generator=g)
+    w = _weights(D, m, seed=N * m + topk)
+    xd = torch.empty(B * N * D + offset, device="cuda")[offset:].view(B, N, D)
+    xd.copy_(x)
+    out = ops.comm_forward(xd, *(t.cuda() for t in w), topk)
+    ref, q, k = oracle.comm_forward(x.numpy(), *(t.numpy() for t in w), topk)
+    ok = ~_near_tie_rows(q, k, topk)
+    assert ok.mean() > 0.99
+    np.testing.assert_allclose(out.cpu().numpy()[ok], ref[ok], rtol=1e-5,
+                               atol=1e-5)

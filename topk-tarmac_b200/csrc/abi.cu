@@ -434,7 +434,8 @@ int tarmac_comm_forward(const float* x, const float* w_qkv, const float* b_qkv,
   const void* ptrs[6] = {x, w_qkv, b_qkv, w_proj, b_proj, out};
   for (const void* ptr : ptrs)
     if (!aligned(ptr, 4)) return TARMAC_ERR_ALIGN;
-  if (comm_smem_bytes(N, in_dim, msg_dim, comm_padded_m(msg_dim)) >
+  if (comm_smem_bytes(N, in_dim, msg_dim, comm_padded_m(msg_dim),
+                      comm_vec(x, w_qkv, in_dim)) >
       (size_t)227 * 1024)
     return TARMAC_ERR_N_TOO_LARGE;
   if (B == 0) return TARMAC_OK;

@@ -32,56 +32,130 @@ __device__ __forceinline__ float gelu_erf(float x) {
   return 0.5f * x * (1.0f + erff(x * 0.70710678118654752f));
 }
 
-// Dynamic shared memory layout (floats): W_proj [m][m], b_proj [m], Q/K/V
-// [N][MP] each (columns m..MP-1 zero), x tile [32][in_dim + 1], and, when
-// p.w_smem, W_qkv [3m][in_dim + 1] (both pads put a warp's 32 reads on
-// distinct banks). Without p.w_smem W_qkv is read from global memory
-// through L1.
-template <int MP, int KM>
-__global__ void __launch_bounds__(COMM_THREADS) comm_forward_kernel(CommParams p) {
+// 4-byte global -> shared copy without a register round trip (cp.async,
+// through L1); completes at cp_async_wait_all().
+__device__ __forceinline__ void cp_async4(float* smem_dst, const float* gsrc) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(d), "l"(gsrc)
+               : "memory");
+}
+
+// Copy rows [0, R) of a row-major [R, D] global matrix into shared rows of DS
+// floats: rows over warps, columns over lanes (no index division). With VEC
+// the rows move as 16-byte pieces (D % 4 == 0, 16-byte aligned source and
+// rows), else as 4-byte words. Every copy is in flight at once; the caller
+// waits with cp_async_wait_all().
+template <bool VEC>
+__device__ __forceinline__ void comm_stage(float* dst, int DS, const float* src,
+                                           int R, int D) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nw = blockDim.x >> 5;
+  if constexpr (VEC) {
+    const int D4 = D >> 2;
+    for (int r = warp; r < R; r += nw)
+      for (int c = lane; c < D4; c += 32)
+        cp_async16(dst + r * DS + 4 * c, src + (int64_t)r * D + 4 * c);
+  } else {
+    for (int r = warp; r < R; r += nw)
+      for (int c = lane; c < D; c += 32)
+        cp_async4(dst + r * DS + c, src + (int64_t)r * D + c);
+  }
+}
+
+// Shared row stride of the x tile and of W_qkv: with VEC, D rounded so that
+// the row stride is an odd number of 16-byte pieces (eight consecutive rows
+// read as 16-byte pieces hit distinct bank groups); else D + 1 (32
+// consecutive rows read word by word hit distinct banks).
+__host__ __device__ __forceinline__ int comm_row_stride(int D, bool vec) {
+  return vec ? 4 * ((D >> 2) | 1) : D + 1;
+}
+
+// Dynamic shared memory layout (floats): Q/K/V [N][MP] each (columns
+// m..MP-1 zero), x tile [32][DS], GELU buffer [COMM_THREADS], W_qkv
+// [3m][DS] when p.w_smem, then W_proj [m][m], b_proj [m], b_qkv [3m].
+// Without p.w_smem W_qkv is read from global memory through L1.
+//
+// Phase 2 runs in one of two forms. An episode with N * MP <= COMM_THREADS
+// (the MAPPO shapes: a handful of agents) gives every (agent, message
+// column) pair its own thread: each thread of an agent's group forms the
+// agent's scores and selection (the same arithmetic in every lane of the
+// group), aggregates its own V column and applies GELU; after a barrier
+// thread (agent, r) forms output column r. Larger episodes give each thread
+// whole query agents. Both forms evaluate every output with the same
+// operations in the same order.
+template <int MP, int KM, bool VEC>
+__global__ void __launch_bounds__(COMM_THREADS, 1) comm_forward_kernel(CommParams p) {
   extern __shared__ __align__(16) float comm_sm[];
   const int N = p.N, D = p.in_dim, m = p.m;
-  const int DS = D + 1;
-  float* spw = comm_sm;
-  float* spb = spw + m * m;
-  float* sq = spb + m;
+  const int DS = comm_row_stride(D, VEC);
+  const int M3 = 3 * m;
+  float* sq = comm_sm;
   float* sk = sq + (size_t)N * MP;
   float* sv = sk + (size_t)N * MP;
   float* sx = sv + (size_t)N * MP;
-  float* sw = sx + (size_t)COMM_XTILE * DS;
+  float* sg = sx + (size_t)COMM_XTILE * DS;
+  float* sw = sg + COMM_THREADS;
+  float* spw = sw + (p.w_smem ? (size_t)M3 * DS : 0);
+  float* spb = spw + m * m;
+  float* sbq = spb + m;
   const int b = blockIdx.x;
   const float* X = p.x + (int64_t)b * N * D;
 
-  for (int e = threadIdx.x; e < m * m; e += blockDim.x) spw[e] = p.wproj[e];
-  for (int e = threadIdx.x; e < m; e += blockDim.x) spb[e] = p.bproj[e];
-  for (int e = threadIdx.x; e < 3 * N * MP; e += blockDim.x) sq[e] = 0.f;
-  if (p.w_smem)
-    for (int e = threadIdx.x; e < 3 * m * D; e += blockDim.x)
-      sw[(e / D) * DS + e % D] = p.wqkv[e];
+  // weights and biases: every copy issued before the first wait
+  if (p.w_smem) comm_stage<VEC>(sw, DS, p.wqkv, M3, D);
+  for (int e = threadIdx.x; e < m * m; e += blockDim.x) cp_async4(spw + e, p.wproj + e);
+  for (int e = threadIdx.x; e < m; e += blockDim.x) cp_async4(spb + e, p.bproj + e);
+  for (int e = threadIdx.x; e < M3; e += blockDim.x) cp_async4(sbq + e, p.bqkv + e);
+  if (m < MP)
+    for (int e = threadIdx.x; e < 3 * N * MP; e += blockDim.x) sq[e] = 0.f;
 
   // ---- phase 1: q, k, v rows of every agent --------------------------------
   // Threads take (row, output) pairs of the staged tile, consecutive threads
   // consecutive outputs of one row: the x row is a broadcast read, the
-  // weight rows distinct banks.
-  const int M3 = 3 * m;
+  // weight rows distinct banks. The dot product runs over the columns in
+  // order, then adds the bias.
   for (int r0 = 0; r0 < N; r0 += COMM_XTILE) {
     const int nr = min(COMM_XTILE, N - r0);
-    __syncthreads();
-    for (int e = threadIdx.x; e < nr * D; e += blockDim.x)
-      sx[(e / D) * DS + e % D] = X[(int64_t)r0 * D + e];
+    __syncthreads();  // the previous tile is consumed
+    comm_stage<VEC>(sx, DS, X + (int64_t)r0 * D, nr, D);
+    cp_async_wait_all();
     __syncthreads();
     for (int pr = threadIdx.x; pr < nr * M3; pr += blockDim.x) {
       const int rr = pr / M3, o = pr - rr * M3;
       const float* xr = sx + rr * DS;
       float acc = 0.f;
-      if (p.w_smem) {
-        const float* wr = sw + o * DS;
-        for (int c = 0; c < D; ++c) acc = fmaf(xr[c], wr[c], acc);
+      if constexpr (VEC) {
+        if (p.w_smem) {
+          const float* wr = sw + o * DS;
+          for (int c = 0; c < D; c += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(xr + c);
+            const float4 w = *reinterpret_cast<const float4*>(wr + c);
+            acc = fmaf(a.x, w.x, acc);
+            acc = fmaf(a.y, w.y, acc);
+            acc = fmaf(a.z, w.z, acc);
+            acc = fmaf(a.w, w.w, acc);
+          }
+        } else {
+          const float4* wr = reinterpret_cast<const float4*>(p.wqkv + (int64_t)o * D);
+          for (int c = 0; c < D; c += 4) {
+            const float4 a = *reinterpret_cast<const float4*>(xr + c);
+            const float4 w = __ldg(wr + (c >> 2));
+            acc = fmaf(a.x, w.x, acc);
+            acc = fmaf(a.y, w.y, acc);
+            acc = fmaf(a.z, w.z, acc);
+            acc = fmaf(a.w, w.w, acc);
+          }
+        }
       } else {
-        const float* wr = p.wqkv + (int64_t)o * D;
-        for (int c = 0; c < D; ++c) acc = fmaf(xr[c], __ldg(wr + c), acc);
+        if (p.w_smem) {
+          const float* wr = sw + o * DS;
+          for (int c = 0; c < D; ++c) acc = fmaf(xr[c], wr[c], acc);
+        } else {
+          const float* wr = p.wqkv + (int64_t)o * D;
+          for (int c = 0; c < D; ++c) acc = fmaf(xr[c], __ldg(wr + c), acc);
+        }
       }
-      acc += __ldg(p.bqkv + o);
+      acc += sbq[o];
       const int part = o / m, col = o - part * m;
       float* dst = part == 0 ? sq : (part == 1 ? sk : sv);
       dst[(r0 + rr) * MP + col] = acc;
@@ -89,7 +163,89 @@ __global__ void __launch_bounds__(COMM_THREADS) comm_forward_kernel(CommParams p
   }
   __syncthreads();
 
-  // ---- phase 2: attention, GELU, projection per query agent ---------------
+  // ---- phase 2: attention, GELU, projection --------------------------------
+  if (N * MP <= COMM_THREADS) {
+    // one thread per (agent i, message column c)
+    const int i = threadIdx.x / MP, c = threadIdx.x % MP;
+    float g = 0.f;
+    if (i < N) {
+      float qi[MP];
+#pragma unroll
+      for (int t = 0; t < MP; t += 4) {
+        const float4 f = *reinterpret_cast<const float4*>(sq + i * MP + t);
+        qi[t] = f.x; qi[t + 1] = f.y; qi[t + 2] = f.z; qi[t + 3] = f.w;
+      }
+      float msg = 0.f;
+      if constexpr (KM > 0) {
+        float bs[KM];
+        int bi[KM];
+#pragma unroll
+        for (int s = 0; s < KM; ++s) {
+          bs[s] = -INFINITY;
+          bi[s] = -1;
+        }
+        for (int j = 0; j < N; ++j) {
+          float s = 0.f;
+#pragma unroll
+          for (int t = 0; t < MP; t += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(sk + j * MP + t);
+            s = fmaf(qi[t], f.x, s);
+            s = fmaf(qi[t + 1], f.y, s);
+            s = fmaf(qi[t + 2], f.z, s);
+            s = fmaf(qi[t + 3], f.w, s);
+          }
+          if (j != i && s > bs[KM - 1]) buf_insert<KM, false>(bs, bi, s, j);
+        }
+        const int kk = p.topk;
+        const float mx = bs[0] * p.scale;
+        float den = 0.f, w[KM];
+#pragma unroll
+        for (int s = 0; s < KM; ++s) {
+          w[s] = (s < kk && bi[s] >= 0) ? expf(bs[s] * p.scale - mx) : 0.f;
+          den += w[s];
+        }
+#pragma unroll
+        for (int s = 0; s < KM; ++s)
+          if (w[s] > 0.f) msg = fmaf(w[s] / den, sv[bi[s] * MP + c], msg);
+      } else {
+        float mref = -INFINITY, l = 0.f;
+        for (int j = 0; j < N; ++j) {
+          if (j == i) continue;
+          float s = 0.f;
+#pragma unroll
+          for (int t = 0; t < MP; t += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(sk + j * MP + t);
+            s = fmaf(qi[t], f.x, s);
+            s = fmaf(qi[t + 1], f.y, s);
+            s = fmaf(qi[t + 2], f.z, s);
+            s = fmaf(qi[t + 3], f.w, s);
+          }
+          s *= p.scale;
+          if (s > mref) {
+            const float a = expf(mref - s);
+            l *= a;
+            msg *= a;
+            mref = s;
+          }
+          const float e = expf(s - mref);
+          l += e;
+          msg = fmaf(e, sv[j * MP + c], msg);
+        }
+        msg *= 1.0f / l;
+      }
+      g = gelu_erf(msg);
+    }
+    sg[threadIdx.x] = g;
+    __syncthreads();
+    if (i < N && c < m) {
+      const float* gr = sg + i * MP;
+      const float* wr = spw + c * m;
+      float acc = 0.f;
+      for (int t = 0; t < m; ++t) acc = fmaf(gr[t], wr[t], acc);
+      p.out[((int64_t)b * N + i) * m + c] = acc + spb[c];
+    }
+    return;
+  }
   for (int i = threadIdx.x; i < N; i += blockDim.x) {
     float qi[MP];
 #pragma unroll
@@ -168,34 +324,47 @@ __global__ void __launch_bounds__(COMM_THREADS) comm_forward_kernel(CommParams p
   }
 }
 
-size_t comm_smem_bytes(int N, int in_dim, int m, int MP) {
-  return sizeof(float) * ((size_t)m * m + m + (size_t)3 * N * MP +
-                          (size_t)COMM_XTILE * (in_dim + 1));
+size_t comm_smem_bytes(int N, int in_dim, int m, int MP, bool vec) {
+  return sizeof(float) * ((size_t)m * m + 4 * (size_t)m + (size_t)3 * N * MP +
+                          (size_t)COMM_XTILE * comm_row_stride(in_dim, vec) +
+                          COMM_THREADS);
+}
+
+bool comm_vec(const float* x, const float* wqkv, int in_dim) {
+  return in_dim % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0 &&
+         reinterpret_cast<uintptr_t>(wqkv) % 16 == 0;
 }
 
 // W_qkv joins the block's shared memory when the total stays within this
 static constexpr size_t COMM_SMEM_WITH_W = 160 * 1024;
 
-template <int MP, int KM>
+template <int MP, int KM, bool VEC>
 static cudaError_t launch_comm_t(CommParams p, cudaStream_t s) {
-  size_t sm = comm_smem_bytes(p.N, p.in_dim, p.m, MP);
-  const size_t wb = sizeof(float) * (size_t)3 * p.m * (p.in_dim + 1);
+  size_t sm = comm_smem_bytes(p.N, p.in_dim, p.m, MP, VEC);
+  const size_t wb =
+      sizeof(float) * (size_t)3 * p.m * comm_row_stride(p.in_dim, VEC);
   p.w_smem = sm + wb <= COMM_SMEM_WITH_W;
   if (p.w_smem) sm += wb;
   cudaError_t e = raise_smem_limit(
-      (const void*)comm_forward_kernel<MP, KM>, (size_t)(sm));
+      (const void*)comm_forward_kernel<MP, KM, VEC>, (size_t)(sm));
   if (e != cudaSuccess) return e;
-  comm_forward_kernel<MP, KM><<<p.B, COMM_THREADS, sm, s>>>(p);
+  comm_forward_kernel<MP, KM, VEC><<<p.B, COMM_THREADS, sm, s>>>(p);
   return cudaGetLastError();
+}
+
+template <int MP, int KM>
+static cudaError_t launch_comm_v(const CommParams& p, cudaStream_t s) {
+  return comm_vec(p.x, p.wqkv, p.in_dim) ? launch_comm_t<MP, KM, true>(p, s)
+                                         : launch_comm_t<MP, KM, false>(p, s);
 }
 
 template <int MP>
 static cudaError_t launch_comm_m(const CommParams& p, cudaStream_t s) {
-  if (p.topk == 0) return launch_comm_t<MP, 0>(p, s);
-  if (p.topk <= 1) return launch_comm_t<MP, 1>(p, s);
-  if (p.topk <= 2) return launch_comm_t<MP, 2>(p, s);
-  if (p.topk <= 4) return launch_comm_t<MP, 4>(p, s);
-  return launch_comm_t<MP, 8>(p, s);
+  if (p.topk == 0) return launch_comm_v<MP, 0>(p, s);
+  if (p.topk <= 1) return launch_comm_v<MP, 1>(p, s);
+  if (p.topk <= 2) return launch_comm_v<MP, 2>(p, s);
+  if (p.topk <= 4) return launch_comm_v<MP, 4>(p, s);
+  return launch_comm_v<MP, 8>(p, s);
 }
 
 // m padded to 8, 16, 32 or 64 columns

@@ -20,7 +20,10 @@ struct CommParams {
 };
 
 cudaError_t launch_comm_forward(const CommParams& p, cudaStream_t s);
-size_t comm_smem_bytes(int N, int in_dim, int m, int MP);
+// dynamic shared memory without the staged W_qkv
+size_t comm_smem_bytes(int N, int in_dim, int m, int MP, bool vec);
+// x and W_qkv rows move as 16-byte pieces
+bool comm_vec(const float* x, const float* wqkv, int in_dim);
 int comm_padded_m(int m);
 
 }  // namespace tarmac

@@ -369,12 +369,16 @@ def comm_forward(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor,
     """gelu(attention(split(x W_qkv^T + b_qkv))) W_proj^T + b_proj in one
     kernel: dense attention for ``topk == 0``, else top-k (k <= 8, lowest
     index on a tie). fp32, inference only (no autograd)."""
+    ts = (x, w_qkv, b_qkv, w_proj, b_proj)
     if not x.is_cuda:
         raise RuntimeError("tarmac_b200 kernels need CUDA tensors")
+    if any(t.device != x.device for t in ts[1:]):
+        raise ValueError("x and the comm weights must be on one device")
     if x.dim() != 3:
         raise ValueError(f"x must be [B, N, in_dim]; got {tuple(x.shape)}")
-    ts = [t.contiguous().float() for t in (x, w_qkv, b_qkv, w_proj, b_proj)]
-    x, w_qkv, b_qkv, w_proj, b_proj = ts
+    x, w_qkv, b_qkv, w_proj, b_proj = (
+        t if t.dtype == torch.float32 and t.is_contiguous()
+        else t.contiguous().float() for t in ts)
     B, N, D = x.shape
     m = w_proj.shape[0]
     if w_qkv.shape != (3 * m, D) or b_qkv.shape != (3 * m,) or \

@@ -4,8 +4,9 @@
         --N 512 --d 16 --k 2 --dtype bf16 --reps 3
 
 Inputs are seeded i.i.d. N(0, 1) Q, K, V (positions U[0, 1)^2 for the
-Morton ops), drawn on the CPU and copied to the device once; every
-repetition is one launch of the selected operation on the current stream.
+Morton ops; for the comm module, x rows of width --in_dim and its
+weights with message width --d), drawn on the CPU and copied to the device
+once; every repetition is one launch of the selected operation on the current stream.
 Prints "ok" and the mean per-call time (CUDA events) on success.
 """
 
@@ -24,12 +25,14 @@ def main() -> int:
     ap.add_argument("--op", default="topk",
                     choices=("topk", "topk_sort", "topk_threshold", "stream",
                              "dense", "morton_prescore", "morton_select",
-                             "prescore"))
+                             "prescore", "comm"))
     ap.add_argument("--B", type=int, default=1024)
     ap.add_argument("--N", type=int, default=512)
     ap.add_argument("--d", type=int, default=16)
     ap.add_argument("--k", type=int, default=2)
     ap.add_argument("--bits", type=int, default=16)
+    ap.add_argument("--in_dim", type=int, default=64,
+                    help="comm op: input width (d is the message width)")
     ap.add_argument("--dtype", default="fp32", choices=("fp32", "bf16"))
     ap.add_argument("--reps", type=int, default=3)
     ap.add_argument("--seed", type=int, default=1)
@@ -46,6 +49,13 @@ def main() -> int:
     pos = torch.rand(a.B, a.N, 2, generator=g).cuda()
     # the Z-order window indices, for the stand-alone prescore op
     widx = ops.morton_select(pos, a.k, bits=a.bits) if a.op == "prescore" else None
+    # the comm module's input rows and weights (Linear-style scaling)
+    if a.op == "comm":
+        x = torch.randn(a.B, a.N, a.in_dim, generator=g).cuda()
+        wq = (torch.randn(3 * a.d, a.in_dim, generator=g) / a.in_dim ** 0.5).cuda()
+        bq = (0.1 * torch.randn(3 * a.d, generator=g)).cuda()
+        wp = (torch.randn(a.d, a.d, generator=g) / a.d ** 0.5).cuda()
+        bp = (0.1 * torch.randn(a.d, generator=g)).cuda()
     calls = {
         "topk": lambda: ops.topk_attention(q, k, v, a.k),
         "topk_sort": lambda: ops.topk_attention(q, k, v, a.k, mode="sort"),
@@ -57,6 +67,7 @@ def main() -> int:
             q, k, v, pos, a.k, bits=a.bits),
         "morton_select": lambda: ops.morton_select(pos, a.k, bits=a.bits),
         "prescore": lambda: ops.prescore_attention(q, k, v, widx),
+        "comm": lambda: ops.comm_forward(x, wq, bq, wp, bp, a.k),
     }
     fn = calls[a.op]
     fn()
