@@ -249,6 +249,33 @@ def _time_loop(fn, steps: int, stream) -> float:
     return e0.elapsed_time(e1)
 
 
+def _graph_us(fn, dev, stream, calls: int = 10, replays: int = 10):
+    """Device time per call: fn(0), ..., fn(calls - 1) captured in one CUDA
+    graph and replayed `replays` times, so no per-call host work (argument
+    checks, output allocation, ctypes) separates the launches. Small problems
+    called one at a time through the API are bound by that host work; this
+    is their device-side figure. None (with the reason) if capture fails."""
+    import torch
+    try:
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        with torch.cuda.stream(side):
+            for s in range(calls):
+                fn(s)
+        stream.wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            for s in range(calls):
+                fn(s)
+        graph.replay()
+        torch.cuda.synchronize(dev)
+        t = _time_loop(lambda s: graph.replay(), replays, stream) / (replays * calls)
+        del graph
+        return round(1e3 * t, 2), None
+    except Exception as e:  # capture unsupported here: report why
+        return None, f"{type(e).__name__}: {e}"
+
+
 def _sweep_c5(ops, dev, stream) -> list:
     """bf16 batch-scaling grid at B=4096 episodes on this GPU: dense and
     top-k (k = 1, 2) through the tensor-core kernels. Informational rows
@@ -316,7 +343,9 @@ def _sweep_c4(ops, dev, stream) -> list:
     kernel (no index tensor), and the two-launch form (selector writing int64
     indices, then the prescore kernel). Inputs rotate over sets larger than
     L2 in total; HBM fraction of the fused kernel from its algorithmic bytes
-    B*N*(8 + 4*d*4) (positions read, Q/K/V read, O written)."""
+    B*N*(8 + 4*d*4) (positions read, Q/K/V read, O written). `*_us` are
+    back-to-back API calls (host-bound for small problems), `fused_dev_us`
+    the same calls replayed from a CUDA graph (device time)."""
     import torch
     peaks = _peaks()
     rows = []
@@ -353,10 +382,14 @@ def _sweep_c4(ops, dev, stream) -> list:
                     fn(s)
                 t = _time_loop(fn, reps, stream) / reps
                 row[name] = round(1e3 * t, 2)
+            row["fused_dev_us"], _ = _graph_us(fused, dev, stream, calls=2 * nsets)
             byts = B * n_ * (8 + 4 * d * 4)
             gbs = byts / (row["fused_us"] * 1e-6) / 1e9
             row["fused_hbm_gbs"] = round(gbs, 1)
             row["fused_hbm_frac"] = round(gbs / peaks["hbm_gbs"], 3)
+            if row["fused_dev_us"]:
+                row["fused_dev_hbm_frac"] = round(
+                    byts / (row["fused_dev_us"] * 1e-6) / 1e9 / peaks["hbm_gbs"], 3)
             row["fused_agent_rows_per_s"] = B * n_ / (row["fused_us"] * 1e-6)
             rows.append(row)
             del sets_
@@ -395,24 +428,9 @@ def _comm_c1(ops, dev, stream) -> dict:
     res["fused_agent_rows_per_s"] = B * N / (res["fused_us"] * 1e-6)
     # the same fused call replayed from a CUDA graph: device time without the
     # per-call host work (argument checks, ctypes)
-    try:
-        side = torch.cuda.Stream(dev)
-        side.wait_stream(stream)
-        with torch.cuda.stream(side):
-            fused(0)
-        stream.wait_stream(side)
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph):
-            for _ in range(20):
-                fused(0)
-        graph.replay()
-        torch.cuda.synchronize(dev)
-        t = _time_loop(lambda s: graph.replay(), 20, stream) / (20 * 20)
-        res["fused_graph_us"] = round(1e3 * t, 2)
-        del graph
-    except Exception as e:  # capture unsupported here: report why
-        res["fused_graph_us"] = None
-        res["graph_note"] = f"{type(e).__name__}: {e}"
+    res["fused_graph_us"], note = _graph_us(fused, dev, stream, calls=20, replays=20)
+    if note:
+        res["graph_note"] = note
     return res
 
 
@@ -578,6 +596,13 @@ def run_ours(args) -> int:
             ops.dense_attention(q_, k_, v_)
             t = _time_loop(lambda s: ops.dense_attention(q_, k_, v_), reps, stream) / reps
             row["dense_us"] = round(1e3 * t, 2)
+            # device time (CUDA graph replay): the API rows above are bound
+            # by the ~14 us host cost per call at small N
+            for kk_ in (1, 2, 4):
+                row[f"topk_k{kk_}_dev_us"], _ = _graph_us(
+                    lambda s: ops.topk_attention(q_, k_, v_, kk_), dev, stream)
+            row["dense_dev_us"], _ = _graph_us(
+                lambda s: ops.dense_attention(q_, k_, v_), dev, stream)
             sweep.append(row)
         del q_, k_, v_
     sweep_c5 = _sweep_c5(ops, dev, stream) if rank == 0 and not args.no_sweep else []

@@ -361,9 +361,8 @@ inline bool chunk_fits(int N, int d, int topk) {
   return sm <= CHUNK_SMEM_MAX;
 }
 
-template <int DP, int KC, bool TIE_HIGH, typename T>
-cudaError_t launch_chunk_t(const AttnParams& p, cudaStream_t s) {
-  constexpr int QPT = chunk_qpt<DP, KC>();
+template <int DP, int KC, bool TIE_HIGH, typename T, int QPT>
+cudaError_t launch_chunk_q(const AttnParams& p, cudaStream_t s) {
   constexpr int CH = chunk_len(KC);
   const int NC = cdiv(p.N, CH);
   const size_t sm = chunk_smem_bytes<DP, QPT, KC, CH>(NC);
@@ -375,6 +374,21 @@ cudaError_t launch_chunk_t(const AttnParams& p, cudaStream_t s) {
   topk_chunk_kernel<DP, QPT, KC, CH, TIE_HIGH, T>
       <<<(unsigned)blocks, CH_WARPS * 32, sm, s>>>(p, NC);
   return cudaGetLastError();
+}
+
+// Queries per lane: the register-budget maximum, lowered for short episodes
+// at d <= 16 so that a block's 32 * QPT query rows do not run far past N
+// (every warp issues the work of all QPT rows per key, live or not, and
+// fewer rows per lane take fewer registers, so more blocks fit an SM).
+template <int DP, int KC, bool TIE_HIGH, typename T>
+cudaError_t launch_chunk_t(const AttnParams& p, cudaStream_t s) {
+  constexpr int QMAX = chunk_qpt<DP, KC>();
+  if constexpr (DP <= 16 && QMAX >= 2) {
+    if (p.N <= 32) return launch_chunk_q<DP, KC, TIE_HIGH, T, 1>(p, s);
+    if constexpr (QMAX >= 4)
+      if (p.N <= 64) return launch_chunk_q<DP, KC, TIE_HIGH, T, 2>(p, s);
+  }
+  return launch_chunk_q<DP, KC, TIE_HIGH, T, QMAX>(p, s);
 }
 
 template <int DP, bool TIE_HIGH, typename T>
