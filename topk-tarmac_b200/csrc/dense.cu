@@ -165,9 +165,8 @@ constexpr int dense_qpt() {
   return DP <= 16 ? 2 : 1;
 }
 
-template <int DP, typename T>
-static cudaError_t launch_dense_dp(const AttnParams& p, cudaStream_t s) {
-  constexpr int QPT = dense_qpt<DP>();
+template <int DP, int QPT, typename T>
+static cudaError_t launch_dense_q(const AttnParams& p, cudaStream_t s) {
   const int groups = cdiv(p.N, 32 * QPT);
   const int wpb = groups < 4 ? groups : 4;
   const int cpe = cdiv(groups, wpb);
@@ -175,6 +174,17 @@ static cudaError_t launch_dense_dp(const AttnParams& p, cudaStream_t s) {
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   dense_kernel<DP, QPT, T><<<(unsigned)blocks, 32 * wpb, 0, s>>>(p);
   return cudaGetLastError();
+}
+
+// One query row per lane for episodes under 128 agents: each episode then
+// spreads over up to four warps instead of one warp walking every key for
+// two rows per lane (the per-row arithmetic does not depend on QPT).
+template <int DP, typename T>
+static cudaError_t launch_dense_dp(const AttnParams& p, cudaStream_t s) {
+  constexpr int QPT = dense_qpt<DP>();
+  if constexpr (QPT > 1)
+    if (p.N < 128) return launch_dense_q<DP, 1, T>(p, s);
+  return launch_dense_q<DP, QPT, T>(p, s);
 }
 
 template <typename T>
