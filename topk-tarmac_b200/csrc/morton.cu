@@ -253,8 +253,10 @@ __device__ __forceinline__ void block_bitonic_sort(
 
 // Bounds, codes and sorted keys of the episode; then ord[r] = agent at curve
 // rank r and rank[i] = curve rank of agent i in shared memory, visible to the
-// whole block on return. red: 4 * MW_WARPS floats; sk: WS*32*P keys.
-template <int WS, int P>
+// whole block on return. NW: the block's first NW (<= MW_WARPS, >= WS) warps
+// hold the agents and exchange the bounds. red: 4 * MW_WARPS floats; sk:
+// WS*32*P keys.
+template <int WS, int P, int NW = MW_WARPS>
 __device__ __forceinline__ void morton_sort_episode_regs(
     const float* pe, int N, int bits, int* ord, int* rank,
     unsigned long long* sk, float* red) {
@@ -281,18 +283,18 @@ __device__ __forceinline__ void morton_sort_episode_regs(
     hx = fmaxf(hx, __shfl_xor_sync(0xffffffffu, hx, o));
     hy = fmaxf(hy, __shfl_xor_sync(0xffffffffu, hy, o));
   }
-  if (lane == 0 && warp < MW_WARPS) {
-    red[warp] = lx; red[MW_WARPS + warp] = ly;
-    red[2 * MW_WARPS + warp] = hx; red[3 * MW_WARPS + warp] = hy;
+  if (lane == 0 && warp < NW) {
+    red[warp] = lx; red[NW + warp] = ly;
+    red[2 * NW + warp] = hx; red[3 * NW + warp] = hy;
   }
   __syncthreads();
-  float bnd[4] = {red[0], red[MW_WARPS], red[2 * MW_WARPS], red[3 * MW_WARPS]};
+  float bnd[4] = {red[0], red[NW], red[2 * NW], red[3 * NW]};
 #pragma unroll
-  for (int w = 1; w < MW_WARPS; ++w) {
+  for (int w = 1; w < NW; ++w) {
     bnd[0] = fminf(bnd[0], red[w]);
-    bnd[1] = fminf(bnd[1], red[MW_WARPS + w]);
-    bnd[2] = fmaxf(bnd[2], red[2 * MW_WARPS + w]);
-    bnd[3] = fmaxf(bnd[3], red[3 * MW_WARPS + w]);
+    bnd[1] = fminf(bnd[1], red[NW + w]);
+    bnd[2] = fmaxf(bnd[2], red[2 * NW + w]);
+    bnd[3] = fmaxf(bnd[3], red[3 * NW + w]);
   }
   unsigned long long key[P];
 #pragma unroll
@@ -341,12 +343,12 @@ __device__ __forceinline__ int window_peer_ord(const int* ord, int r, int o,
 // clustered or duplicated positions) takes the bitonic network instead.
 constexpr int BUCKET_MAX = 32;
 
-// Exclusive scan of a[0..M) in place by the first MW_THREADS threads; every
+// Exclusive scan of a[0..M) in place by the first 32 * NW threads; every
 // thread of the block calls it and gets the largest entry. wsum: 2 *
-// MW_WARPS ints of shared memory.
-template <int M>
+// MW_WARPS ints of shared memory (NW <= MW_WARPS).
+template <int M, int NW = MW_WARPS>
 __device__ __forceinline__ int block_scan_max(int* a, int* wsum) {
-  constexpr int V = M >= MW_THREADS ? M / MW_THREADS : 1;
+  constexpr int V = M >= (32 * NW) ? M / (32 * NW) : 1;
   const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
   const int base = t * V;
   const bool has = base < M;
@@ -367,16 +369,16 @@ __device__ __forceinline__ int block_scan_max(int* a, int* wsum) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1)
     mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  if (warp < MW_WARPS) {
+  if (warp < NW) {
     if (lane == 31) wsum[warp] = inc;
-    if (lane == 0) wsum[MW_WARPS + warp] = mx;
+    if (lane == 0) wsum[NW + warp] = mx;
   }
   __syncthreads();
   int off = 0, gmx = 0;
 #pragma unroll
-  for (int w = 0; w < MW_WARPS; ++w) {
+  for (int w = 0; w < NW; ++w) {
     off += w < warp ? wsum[w] : 0;
-    gmx = max(gmx, wsum[MW_WARPS + w]);
+    gmx = max(gmx, wsum[NW + w]);
   }
   int run = off + inc - sum;
   if (has) {
@@ -390,9 +392,10 @@ __device__ __forceinline__ int block_scan_max(int* a, int* wsum) {
   return gmx;
 }
 
-// Same result as morton_sort_episode_regs (ord, rank; sk and red as there).
-// Shared scratch: code[M], bst[M], memb[M], wsum[2 * MW_WARPS].
-template <int WS, int P>
+// Same result as morton_sort_episode_regs (ord, rank; sk and red as there;
+// the block's first NW warps hold the agents). Shared scratch: code[M],
+// bst[M], memb[M], wsum[2 * MW_WARPS].
+template <int WS, int P, int NW = MW_WARPS>
 __device__ __forceinline__ void morton_order_episode(
     const float* pe, int N, int bits, int* ord, int* rank,
     unsigned long long* sk, float* red, uint32_t* code, int* bst, int* memb,
@@ -400,16 +403,16 @@ __device__ __forceinline__ void morton_order_episode(
   constexpr int M = WS * 32 * P;
   constexpr int LB = M >= 1024 ? 10 : M >= 512 ? 9 : M >= 256 ? 8
                    : M >= 128 ? 7 : M >= 64 ? 6 : 5;
-  constexpr int EPT = (M + MW_THREADS - 1) / MW_THREADS;
+  constexpr int EPT = (M + (32 * NW) - 1) / (32 * NW);
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // the first MW_THREADS threads hold the agents; any further threads of a
+  // the first (32 * NW) threads hold the agents; any further threads of a
   // larger block only take part in the barriers
-  const bool srt = tid < MW_THREADS;
+  const bool srt = tid < (32 * NW);
   float2 xy[EPT];
   float lx = INFINITY, ly = INFINITY, hx = -INFINITY, hy = -INFINITY;
 #pragma unroll
   for (int t = 0; t < EPT; ++t) {
-    const int e = tid + MW_THREADS * t;
+    const int e = tid + (32 * NW) * t;
     xy[t] = (srt && e < N) ? reinterpret_cast<const float2*>(pe)[e]
                            : make_float2(0.f, 0.f);
     if (srt && e < N) {
@@ -418,7 +421,7 @@ __device__ __forceinline__ void morton_order_episode(
     }
   }
   if (srt)
-    for (int e = tid; e < M; e += MW_THREADS) bst[e] = 0;
+    for (int e = tid; e < M; e += (32 * NW)) bst[e] = 0;
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
     lx = fminf(lx, __shfl_xor_sync(0xffffffffu, lx, o));
@@ -426,18 +429,18 @@ __device__ __forceinline__ void morton_order_episode(
     hx = fmaxf(hx, __shfl_xor_sync(0xffffffffu, hx, o));
     hy = fmaxf(hy, __shfl_xor_sync(0xffffffffu, hy, o));
   }
-  if (lane == 0 && warp < MW_WARPS) {
-    red[warp] = lx; red[MW_WARPS + warp] = ly;
-    red[2 * MW_WARPS + warp] = hx; red[3 * MW_WARPS + warp] = hy;
+  if (lane == 0 && warp < NW) {
+    red[warp] = lx; red[NW + warp] = ly;
+    red[2 * NW + warp] = hx; red[3 * NW + warp] = hy;
   }
   __syncthreads();
-  float bnd[4] = {red[0], red[MW_WARPS], red[2 * MW_WARPS], red[3 * MW_WARPS]};
+  float bnd[4] = {red[0], red[NW], red[2 * NW], red[3 * NW]};
 #pragma unroll
-  for (int w = 1; w < MW_WARPS; ++w) {
+  for (int w = 1; w < NW; ++w) {
     bnd[0] = fminf(bnd[0], red[w]);
-    bnd[1] = fminf(bnd[1], red[MW_WARPS + w]);
-    bnd[2] = fmaxf(bnd[2], red[2 * MW_WARPS + w]);
-    bnd[3] = fmaxf(bnd[3], red[3 * MW_WARPS + w]);
+    bnd[1] = fminf(bnd[1], red[NW + w]);
+    bnd[2] = fmaxf(bnd[2], red[2 * NW + w]);
+    bnd[3] = fmaxf(bnd[3], red[3 * NW + w]);
   }
   // the code has 2 * bits significant bits; its leading LB name the bucket
   const int shift = 2 * bits > LB ? 2 * bits - LB : 0;
@@ -445,7 +448,7 @@ __device__ __forceinline__ void morton_order_episode(
   int bk[EPT], slot[EPT];
 #pragma unroll
   for (int t = 0; t < EPT; ++t) {
-    const int e = tid + MW_THREADS * t;
+    const int e = tid + (32 * NW) * t;
     if (srt && e < N) {
       c[t] = morton_of(xy[t], bnd, bits);
       code[e] = c[t];
@@ -454,20 +457,20 @@ __device__ __forceinline__ void morton_order_episode(
     }
   }
   __syncthreads();
-  const int most = block_scan_max<M>(bst, wsum);
+  const int most = block_scan_max<M, NW>(bst, wsum);
   if (most > BUCKET_MAX) {  // block-uniform
-    morton_sort_episode_regs<WS, P>(pe, N, bits, ord, rank, sk, red);
+    morton_sort_episode_regs<WS, P, NW>(pe, N, bits, ord, rank, sk, red);
     return;
   }
 #pragma unroll
   for (int t = 0; t < EPT; ++t) {
-    const int e = tid + MW_THREADS * t;
+    const int e = tid + (32 * NW) * t;
     if (srt && e < N) memb[bst[bk[t]] + slot[t]] = e;
   }
   __syncthreads();
 #pragma unroll
   for (int t = 0; t < EPT; ++t) {
-    const int e = tid + MW_THREADS * t;
+    const int e = tid + (32 * NW) * t;
     if (srt && e < N) {
       const int lo = bst[bk[t]];
       const int hi = bk[t] + 1 < M ? bst[bk[t] + 1] : N;
@@ -610,7 +613,8 @@ __global__ void __launch_bounds__(MW_THREADS) morton_prescore_regs_kernel(
 // the row index, so the pieces a warp gathers from 32 random rows spread
 // over all 8 bank groups. Dynamic shared memory: K then V, N rows of DT
 // elements each. The block has up to 256 threads, one or two query rows per
-// thread; the sort runs on its first four warps.
+// thread; the sort runs on its first four warps (on all of them in the 32-
+// and 64-thread blocks of episodes up to 32 and 64 agents).
 template <int WS, int P, int DT, typename T, int NT>
 __global__ void __launch_bounds__(NT) morton_prescore_smem_kernel(
     AttnParams p, const float* __restrict__ pos, int bits,
@@ -631,9 +635,11 @@ __global__ void __launch_bounds__(NT) morton_prescore_smem_kernel(
   const int b = blockIdx.x;
   const uint32_t sK = tc_smem_base(kv_smem);
   const uint32_t sV = sK + (uint32_t)N * CPR * 16u;
+  constexpr int NW = NT / 32 < MW_WARPS ? NT / 32 : MW_WARPS;
+  static_assert(NW >= WS, "the sorting warps must exist");
   stage_kv_episode<DT, T, NT>(p, b, sK, sV);
-  morton_order_episode<WS, P>(pos + (int64_t)b * N * 2, N, bits, ord, rank, sk,
-                              red, code, bst, memb, wsum);
+  morton_order_episode<WS, P, NW>(pos + (int64_t)b * N * 2, N, bits, ord,
+                                  rank, sk, red, code, bst, memb, wsum);
   cp_async_wait<0>();
   __syncthreads();
   const T* Qb = static_cast<const T*>(p.q) + (int64_t)b * p.st.qb;
@@ -705,12 +711,15 @@ static cudaError_t launch_mpr(const AttnParams& p, const float* pos, int bits,
 
 // NT = half the sort's key count, at least 128 threads (one or two query
 // rows per thread): with the 64 KB of K and V at N = 512, three blocks fit
-// an SM, so one block's sort runs beside another's attention rows
+// an SM, so one block's sort runs beside another's attention rows. Episodes
+// of up to 32 or 64 agents take a block of exactly 32 or 64 threads (one
+// row per thread, no idle lanes), so twice or four times as many episodes
+// are resident per SM.
 template <int WS, int P, int DT, typename T>
 static cudaError_t launch_mps(const AttnParams& p, const float* pos, int bits,
                               int64_t* idx_out, cudaStream_t s) {
   constexpr int M = WS * 32 * P;
-  constexpr int NT = M / 2 < MW_THREADS ? MW_THREADS : M / 2;
+  constexpr int NT = M <= 64 ? M : (M / 2 < MW_THREADS ? MW_THREADS : M / 2);
   const size_t sm = (size_t)2 * p.N * DT * sizeof(T);
   cudaError_t e = raise_smem_limit(
       (const void*)morton_prescore_smem_kernel<WS, P, DT, T, NT>, (size_t)(sm));
