@@ -1,8 +1,8 @@
 """Torch-facing launchers over the C ABI.
 
-Each function takes CUDA tensors, checks them, allocates the output with
-``torch.empty`` (the C ABI itself never allocates) and launches on the current
-stream of the tensors' device. Q, K, V are ``[B, N, d]`` fp32 or bf16 tensors
+Each function takes CUDA tensors, checks them, allocates the output
+(``torch.empty_like`` / ``torch.empty``; the C ABI itself never allocates) and
+launches on the current stream of the tensors' device. Q, K, V are ``[B, N, d]`` fp32 or bf16 tensors
 with a unit innermost stride; other strides (e.g. the ``qkv.chunk(3, -1)``
 views of the comm module) are passed through without a copy. Nothing here
 computes on the CPU: a CPU tensor or a missing library is an error.
@@ -15,7 +15,7 @@ diagonal excluded, softmax over the retained peers, weighted sum of V rows.
 from __future__ import annotations
 
 import contextlib
-import ctypes
+import struct
 
 import torch
 
@@ -83,11 +83,22 @@ def _check_qkv(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor):
     return _unit_inner(q), _unit_inner(k), _unit_inner(v)
 
 
-def _strides(q, k, v, o) -> ctypes.Array:
-    arr = (ctypes.c_int64 * 8)(q.stride(0), q.stride(1), k.stride(0),
-                               k.stride(1), v.stride(0), v.stride(1),
-                               o.stride(0), o.stride(1))
-    return arr
+def _strides(q, k, v, o) -> bytes:
+    """Batch and row strides of q, k, v, o as the int64[8] the C ABI reads.
+    A bytes object passes as a pointer to its buffer and lives as long as
+    the call's arguments; packing costs well under the eight-element ctypes
+    array it replaces (host cost per call matters for small problems)."""
+    sq, sk, sv, so = q.stride(), k.stride(), v.stride(), o.stride()
+    return _PACK8(sq[0], sq[1], sk[0], sk[1], sv[0], sv[1], so[0], so[1])
+
+
+_PACK8 = struct.Struct("=8q").pack
+_CONTIG = torch.contiguous_format
+
+
+def _empty_as(q: torch.Tensor) -> torch.Tensor:
+    """A contiguous output of q's shape, dtype and device."""
+    return torch.empty_like(q, memory_format=_CONTIG)
 
 
 def _scale(d: int, scale: float | None) -> float:
@@ -99,13 +110,13 @@ def dense_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     """softmax(q k^T * scale, diagonal excluded) v."""
     q, k, v = _check_qkv(q, k, v)
     B, N, d = q.shape
-    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    out = _empty_as(q)
     if N < 2:
         return out.fill_(float("nan"))
-    strides = _strides(q, k, v, out)  # must outlive the call
+    strides = _strides(q, k, v, out)
     with _on(q.device):
         _lib.call("tarmac_dense_attention", _ptr(q), _ptr(k), _ptr(v),
-                  _ptr(out), ctypes.addressof(strides), B, N, d,
+                  _ptr(out), strides, B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), _stream(q.device))
     return out
 
@@ -125,13 +136,13 @@ def topk_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     B, N, d = q.shape
     if mode not in _MODES:
         raise ValueError(f"unknown selection mode {mode!r}")
-    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    out = _empty_as(q)
     idx = (torch.empty((B, N, topk), device=q.device, dtype=torch.int32)
            if return_indices else None)
     strides = _strides(q, k, v, out)
     with _on(q.device):
         _lib.call("tarmac_topk_attention", _ptr(q), _ptr(k), _ptr(v),
-                  _ptr(out), ctypes.addressof(strides), B, N, d,
+                  _ptr(out), strides, B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), int(topk), _MODES[mode],
                   _ptr(idx), _stream(q.device))
     return (out, idx) if return_indices else out
@@ -145,13 +156,13 @@ def streaming_topk_attention(q: torch.Tensor, k: torch.Tensor,
     through shared memory; no cap on N."""
     q, k, v = _check_qkv(q, k, v)
     B, N, d = q.shape
-    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    out = _empty_as(q)
     idx = (torch.empty((B, N, topk), device=q.device, dtype=torch.int32)
            if return_indices else None)
     strides = _strides(q, k, v, out)
     with _on(q.device):
         _lib.call("tarmac_streaming_topk_attention", _ptr(q), _ptr(k), _ptr(v),
-                  _ptr(out), ctypes.addressof(strides), B, N, d,
+                  _ptr(out), strides, B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), int(topk), _ptr(idx),
                   _stream(q.device))
     return (out, idx) if return_indices else out
@@ -172,13 +183,13 @@ def prescore_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         raise ValueError("idx must be on the device of q")
     idx = idx.contiguous()
     kk = idx.shape[-1]
-    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    out = _empty_as(q)
     if kk == 0:
         return out.fill_(float("nan"))
     strides = _strides(q, k, v, out)
     with _on(q.device):
         _lib.call("tarmac_prescore_attention", _ptr(q), _ptr(k), _ptr(v),
-                  _ptr(out), ctypes.addressof(strides), _ptr(idx),
+                  _ptr(out), strides, _ptr(idx),
                   int(idx.dtype == torch.int64), kk, B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), _stream(q.device))
     return out
@@ -226,13 +237,13 @@ def morton_prescore_attention(q: torch.Tensor, k: torch.Tensor,
     B, N, d = q.shape
     if tuple(pos.shape[:2]) != (B, N):
         raise ValueError("pos must be [B, N, 2] matching q")
-    out = torch.empty((B, N, d), device=q.device, dtype=q.dtype)
+    out = _empty_as(q)
     idx = (torch.empty((B, N, topk), device=q.device, dtype=torch.int64)
            if return_indices else None)
     strides = _strides(q, k, v, out)
     with _on(q.device):
         _lib.call("tarmac_morton_prescore_attention", _ptr(q), _ptr(k),
-                  _ptr(v), _ptr(out), ctypes.addressof(strides), _ptr(pos),
+                  _ptr(v), _ptr(out), strides, _ptr(pos),
                   B, N, d, _DTYPES[q.dtype], _scale(d, scale), int(topk),
                   int(bits), _ptr(idx), _stream(q.device))
     return (out, idx) if return_indices else out
@@ -242,11 +253,12 @@ def morton_prescore_attention(q: torch.Tensor, k: torch.Tensor,
 # gradients (training path)
 # ---------------------------------------------------------------------------
 
-def _strides_n(*ts) -> ctypes.Array:
+def _strides_n(*ts) -> bytes:
     vals = []
     for t in ts:
-        vals += [t.stride(0), t.stride(1)]
-    return (ctypes.c_int64 * len(vals))(*vals)
+        st = t.stride()
+        vals += [st[0], st[1]]
+    return struct.pack(f"={len(vals)}q", *vals)
 
 
 def gather_attention_backward(q: torch.Tensor, k: torch.Tensor,
@@ -275,7 +287,7 @@ def gather_attention_backward(q: torch.Tensor, k: torch.Tensor,
     strides = _strides_n(q, k, v, dout)
     with _on(q.device):
         _lib.call("tarmac_gather_attention_backward", _ptr(q), _ptr(k),
-                  _ptr(v), _ptr(dout), ctypes.addressof(strides), _ptr(idx),
+                  _ptr(v), _ptr(dout), strides, _ptr(idx),
                   int(idx.dtype == torch.int64), idx.shape[-1], B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), _ptr(dq), _ptr(dk),
                   _ptr(dv), _stream(q.device))
@@ -303,7 +315,7 @@ def dense_attention_backward(q: torch.Tensor, k: torch.Tensor,
     strides = _strides_n(q, k, v, out, dout)
     with _on(q.device):
         _lib.call("tarmac_dense_attention_backward", _ptr(q), _ptr(k), _ptr(v),
-                  _ptr(out), _ptr(dout), ctypes.addressof(strides), B, N, d,
+                  _ptr(out), _ptr(dout), strides, B, N, d,
                   _DTYPES[q.dtype], _scale(d, scale), _ptr(dq), _ptr(dk),
                   _ptr(dv), _ptr(work), _stream(q.device))
     return dq, dk, dv
