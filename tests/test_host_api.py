@@ -125,3 +125,28 @@ def test_launch_form_shim_maps_arguments(monkeypatch):
     assert seen == dict(shape=(B, N, d), stride=(N * 3 * d, 3 * d, 1), topk=3,
                         mode="argmax", scale=0.25)
     assert (o == 1).all()
+
+
+def test_stride_buffer_layout(monkeypatch):
+    """The launchers pass q, k, v, out batch and row strides as the int64[8]
+    the C ABI reads (include/tarmac_b200.h): packed bytes in that order, out
+    contiguous; checked on CPU with the library call captured."""
+    import struct
+
+    import torch
+    from tarmac_b200 import _lib, ops
+
+    seen = {}
+    monkeypatch.setattr(_lib, "call", lambda name, *a: seen.setdefault(name, a))
+    monkeypatch.setattr(ops, "_check_qkv", lambda q, k, v: (q, k, v))
+    monkeypatch.setattr(ops, "_on", lambda dev: ops._SAME_DEVICE)
+    monkeypatch.setattr(ops, "_stream", lambda dev: 0)
+    base = torch.randn(3, 5, 3 * 8)
+    q, k, v = base.chunk(3, dim=-1)              # row stride 24, batch 120
+    out = ops.topk_attention(q, k, v, 2)
+    assert out.is_contiguous() and out.shape == (3, 5, 8)
+    args = seen["tarmac_topk_attention"]
+    strides = struct.unpack("=8q", args[4])
+    assert strides == (120, 24, 120, 24, 120, 24, 40, 8)
+    assert args[3] == out.data_ptr() and args[0] == q.data_ptr()
+    assert struct.unpack("=4q", ops._strides_n(q, out)) == (120, 24, 40, 8)
