@@ -8,8 +8,11 @@
 // episode's keys, a merge, then a finalisation on some of the warps) leaves
 // most of each block waiting on memory latency. Here:
 //
-// * ceil(N / 32) warps own one episode, one query row per lane, and a block
-//   of four warps carries 4, 2 or 1 episodes. The episode's warps copy its K
+// * Up to 64 agents, ceil(N / 16) warps own one episode, two lanes per query
+//   row (each scores every other key and keeps its own k best; the pair then
+//   merges the two buffers by shuffles and each lane stores half the row);
+//   above 64 agents, four warps, one lane per row. A block of four warps
+//   carries 4, 2 or 1 episodes. The episode's warps copy its K
 //   and V rows into shared memory (16-byte cp.async for aligned fp32 rows,
 //   converted through registers otherwise; rows padded to DP + 4 floats)
 //   while each lane's Q row loads into registers.
@@ -40,22 +43,26 @@ __device__ __forceinline__ float4 small_cols4(const T* src, int c, int d,
   return f;
 }
 
-template <int KC, int WPE, bool TIE_HIGH, typename T>
+template <int KC, int WPE, int SPLIT, bool TIE_HIGH, typename T>
 __global__ void __launch_bounds__(SMALL_WARPS * 32)
     topk_small_kernel(AttnParams p) {
   constexpr int DP = SMALL_DP;
   constexpr int EPB = SMALL_WARPS / WPE;  // episodes per block
-  constexpr int ROWS = WPE * 32;          // rows an episode's warps hold
+  constexpr int GT = WPE * 32;            // threads of an episode
+  constexpr int ROWS = GT / SPLIT;        // rows (= query rows) it holds
   constexpr int KS = DP + 4;
   constexpr int C4 = DP / 4;
+  static_assert(SPLIT == 1 || SPLIT == 2, "one or two lanes per query row");
   __shared__ __align__(16) float sk[EPB][ROWS * KS];
   __shared__ __align__(16) float sv[EPB][ROWS * KS];
 
   const int N = p.N, d = p.d;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
   const int e = warp / WPE;
   const int64_t b = (int64_t)blockIdx.x * EPB + e;
-  const int i = (warp - e * WPE) * 32 + lane;
+  const int t = threadIdx.x - e * GT;  // thread within the episode
+  const int i = t / SPLIT;             // its query row
+  const int h = t % SPLIT;             // its share of the keys
   const bool has = b < p.B;
   const bool live = has && i < N;
   const bool vec = p.vec != 0;
@@ -69,7 +76,7 @@ __global__ void __launch_bounds__(SMALL_WARPS * 32)
 
   // ---- the episode's K and V rows into shared memory ----------------------
   if (has) {
-    for (int x = threadIdx.x - e * ROWS; x < N * C4; x += ROWS) {
+    for (int x = t; x < N * C4; x += GT) {
       const int r = x / C4, c = (x % C4) * 4;
       float* dk = sK + r * KS + c;
       float* dv = sV + r * KS + c;
@@ -108,7 +115,6 @@ __global__ void __launch_bounds__(SMALL_WARPS * 32)
   }
   cp_async_wait_all();
   __syncthreads();
-  if (!live) return;
 
   // ---- scores and the k best by (score, index) -----------------------------
   float bs[KC];
@@ -118,12 +124,33 @@ __global__ void __launch_bounds__(SMALL_WARPS * 32)
     bs[m] = -INFINITY;
     bi[m] = -1;
   }
+  if (live) {
 #pragma unroll 4
-  for (int j = 0; j < N; ++j) {
-    const float s = dot_pairs<DP>(qf, sK + j * KS);
-    if (j != i && s == s && better<TIE_HIGH>(s, j, bs[KC - 1], bi[KC - 1]))
-      ins_idx<KC, TIE_HIGH>(bs, bi, s, j);
+    for (int j = h; j < N; j += SPLIT) {
+      const float s = dot_pairs<DP>(qf, sK + j * KS);
+      if (j != i && s == s && better<TIE_HIGH>(s, j, bs[KC - 1], bi[KC - 1]))
+        ins_idx<KC, TIE_HIGH>(bs, bi, s, j);
+    }
   }
+  if constexpr (SPLIT == 2) {
+    // The pair's buffers hold disjoint keys: each lane merges its partner's
+    // into its own by the same (score, index) order, so both end with the k
+    // best of the whole row in the same order. Every lane of the warp takes
+    // part in the shuffles (lanes past N carry empty buffers); the two lanes
+    // of a pair share one query row, so both are live or neither.
+    float ps[KC];
+    int pi[KC];
+#pragma unroll
+    for (int m = 0; m < KC; ++m) {
+      ps[m] = __shfl_xor_sync(0xffffffffu, bs[m], 1);
+      pi[m] = __shfl_xor_sync(0xffffffffu, bi[m], 1);
+    }
+#pragma unroll
+    for (int m = 0; m < KC; ++m)
+      if (pi[m] >= 0 && better<TIE_HIGH>(ps[m], pi[m], bs[KC - 1], bi[KC - 1]))
+        ins_idx<KC, TIE_HIGH>(bs, bi, ps[m], pi[m]);
+  }
+  if (!live) return;
 
   // ---- softmax over the k retained scores, V gather-aggregate -------------
   const int kk = p.topk;
@@ -159,8 +186,19 @@ __global__ void __launch_bounds__(SMALL_WARPS * 32)
 #pragma unroll
     for (int c = 0; c < DP; ++c) acc[c] = __int_as_float(0x7fc00000);
   }
-  store_row<DP, T>(O + (int64_t)i * p.st.on, acc, d, vec);
-  if (p.idx_out != nullptr) {
+  if constexpr (SPLIT == 1) {
+    store_row<DP, T>(O + (int64_t)i * p.st.on, acc, d, vec);
+  } else {
+    // each lane of the pair stores half of the row's columns
+    constexpr int HW = DP / 2;
+    float half[HW];
+#pragma unroll
+    for (int c = 0; c < HW; ++c) half[c] = h ? acc[HW + c] : acc[c];
+    if (d > h * HW)
+      store_row<HW, T>(O + (int64_t)i * p.st.on + h * HW, half, d - h * HW,
+                       vec);
+  }
+  if (p.idx_out != nullptr && h == 0) {
     int32_t* io = p.idx_out + ((int64_t)bb * N + i) * kk;
 #pragma unroll
     for (int m = 0; m < KC; ++m)
@@ -168,21 +206,24 @@ __global__ void __launch_bounds__(SMALL_WARPS * 32)
   }
 }
 
-template <int KC, int WPE, bool TIE_HIGH, typename T>
+template <int KC, int WPE, int SPLIT, bool TIE_HIGH, typename T>
 static cudaError_t launch_small_w(const AttnParams& p, cudaStream_t s) {
   constexpr int EPB = SMALL_WARPS / WPE;
   const int64_t blocks = ((int64_t)p.B + EPB - 1) / EPB;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  topk_small_kernel<KC, WPE, TIE_HIGH, T>
+  topk_small_kernel<KC, WPE, SPLIT, TIE_HIGH, T>
       <<<(unsigned)blocks, SMALL_WARPS * 32, 0, s>>>(p);
   return cudaGetLastError();
 }
 
+// Up to 64 agents a query row takes two lanes (each scores every other key;
+// twice the warps, half the chain per lane); above, one lane.
 template <int KC, bool TIE_HIGH, typename T>
 static cudaError_t launch_small_n(const AttnParams& p, cudaStream_t s) {
-  if (p.N <= 32) return launch_small_w<KC, 1, TIE_HIGH, T>(p, s);
-  if (p.N <= 64) return launch_small_w<KC, 2, TIE_HIGH, T>(p, s);
-  return launch_small_w<KC, 4, TIE_HIGH, T>(p, s);
+  if (p.N <= 16) return launch_small_w<KC, 1, 2, TIE_HIGH, T>(p, s);
+  if (p.N <= 32) return launch_small_w<KC, 2, 2, TIE_HIGH, T>(p, s);
+  if (p.N <= 64) return launch_small_w<KC, 4, 2, TIE_HIGH, T>(p, s);
+  return launch_small_w<KC, 4, 1, TIE_HIGH, T>(p, s);
 }
 
 template <bool TIE_HIGH, typename T>
