@@ -8,11 +8,11 @@
 // episode's keys, a merge, then a finalisation on some of the warps) leaves
 // most of each block waiting on memory latency. Here:
 //
-// * Up to 64 agents, ceil(N / 16) warps own one episode, two lanes per query
-//   row (each scores every other key and keeps its own k best; the pair then
-//   merges the two buffers by shuffles and each lane stores half the row);
-//   above 64 agents, four warps, one lane per row. A block of four warps
-//   carries 4, 2 or 1 episodes. The episode's warps copy its K
+// * Up to 64 agents, ceil(N / 16) warps own one episode with two lanes per
+//   query row (each scores every other key and keeps its own k best; the
+//   pair then merges the two buffers by shuffles and each lane stores half
+//   the row), and a block of four warps carries 4, 2 or 1 episodes. Above 64
+//   agents, four warps own one episode, one lane per row. The episode's warps copy its K
 //   and V rows into shared memory (16-byte cp.async for aligned fp32 rows,
 //   converted through registers otherwise; rows padded to DP + 4 floats)
 //   while each lane's Q row loads into registers.
@@ -27,9 +27,8 @@
 
 namespace tarmac {
 
-constexpr int SMALL_WARPS = 4;
 constexpr int SMALL_DP = 16;
-constexpr int SMALL_MAX_N = SMALL_WARPS * 32;
+constexpr int SMALL_MAX_N = 128;
 
 template <typename T>
 __device__ __forceinline__ float4 small_cols4(const T* src, int c, int d,
@@ -43,11 +42,11 @@ __device__ __forceinline__ float4 small_cols4(const T* src, int c, int d,
   return f;
 }
 
-template <int KC, int WPE, int SPLIT, bool TIE_HIGH, typename T>
-__global__ void __launch_bounds__(SMALL_WARPS * 32)
+template <int KC, int WPE, int SPLIT, int BW, bool TIE_HIGH, typename T>
+__global__ void __launch_bounds__(BW * 32)
     topk_small_kernel(AttnParams p) {
   constexpr int DP = SMALL_DP;
-  constexpr int EPB = SMALL_WARPS / WPE;  // episodes per block
+  constexpr int EPB = BW / WPE;           // episodes per block
   constexpr int GT = WPE * 32;            // threads of an episode
   constexpr int ROWS = GT / SPLIT;        // rows (= query rows) it holds
   constexpr int KS = DP + 4;
@@ -206,24 +205,27 @@ __global__ void __launch_bounds__(SMALL_WARPS * 32)
   }
 }
 
-template <int KC, int WPE, int SPLIT, bool TIE_HIGH, typename T>
+template <int KC, int WPE, int SPLIT, int BW, bool TIE_HIGH, typename T>
 static cudaError_t launch_small_w(const AttnParams& p, cudaStream_t s) {
-  constexpr int EPB = SMALL_WARPS / WPE;
+  constexpr int EPB = BW / WPE;
   const int64_t blocks = ((int64_t)p.B + EPB - 1) / EPB;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  topk_small_kernel<KC, WPE, SPLIT, TIE_HIGH, T>
-      <<<(unsigned)blocks, SMALL_WARPS * 32, 0, s>>>(p);
+  topk_small_kernel<KC, WPE, SPLIT, BW, TIE_HIGH, T>
+      <<<(unsigned)blocks, BW * 32, 0, s>>>(p);
   return cudaGetLastError();
 }
 
-// Up to 64 agents a query row takes two lanes (each scores every other key;
-// twice the warps, half the chain per lane); above, one lane.
+// Up to 64 agents a query row takes two lanes (each scores every other
+// key: twice the warps, half the chain per lane) and a block of four warps
+// carries 4, 2 or 1 episodes. Above, one lane per row in a four-warp block:
+// two lanes per row in eight-warp blocks measured slower there (N=100, k=2:
+// 22.7 -> 25.7 us at B=1024).
 template <int KC, bool TIE_HIGH, typename T>
 static cudaError_t launch_small_n(const AttnParams& p, cudaStream_t s) {
-  if (p.N <= 16) return launch_small_w<KC, 1, 2, TIE_HIGH, T>(p, s);
-  if (p.N <= 32) return launch_small_w<KC, 2, 2, TIE_HIGH, T>(p, s);
-  if (p.N <= 64) return launch_small_w<KC, 4, 2, TIE_HIGH, T>(p, s);
-  return launch_small_w<KC, 4, 1, TIE_HIGH, T>(p, s);
+  if (p.N <= 16) return launch_small_w<KC, 1, 2, 4, TIE_HIGH, T>(p, s);
+  if (p.N <= 32) return launch_small_w<KC, 2, 2, 4, TIE_HIGH, T>(p, s);
+  if (p.N <= 64) return launch_small_w<KC, 4, 2, 4, TIE_HIGH, T>(p, s);
+  return launch_small_w<KC, 4, 1, 4, TIE_HIGH, T>(p, s);
 }
 
 template <bool TIE_HIGH, typename T>
