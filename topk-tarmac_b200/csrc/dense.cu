@@ -23,16 +23,17 @@ __host__ __device__ constexpr int dense_tile_keys() {
   return 8192 / (DP * 4);  // 8 KB of K plus 8 KB of V per tile
 }
 
-// One staged tile of nk keys (rows of DP floats) against QPT query rows.
-template <int DP, int QPT>
+// One staged tile of nk keys (rows of DP floats) against QPT query rows;
+// with SPLIT = 2 this lane takes the keys of parity h only.
+template <int DP, int QPT, int SPLIT>
 __device__ __forceinline__ void dense_tile(
     const float* __restrict__ sk, const float* __restrict__ sv, int nk, int t0,
     const int (&qi)[QPT], const uint64_t (&qp)[QPT][DP / 2],
     uint64_t (&acc)[QPT][DP / 2], float (&mc2)[QPT], float (&mth)[QPT],
-    float (&l)[QPT], float c2) {
+    float (&l)[QPT], float c2, int h) {
   constexpr int H = DP / 2;
 #pragma unroll 2
-  for (int jj = 0; jj < nk; ++jj) {
+  for (int jj = h; jj < nk; jj += SPLIT) {
     const float* kr = sk + jj * DP;
     const float* vr = sv + jj * DP;
     const int j = t0 + jj;
@@ -51,7 +52,7 @@ __device__ __forceinline__ void dense_tile(
         l[r] *= alpha;
         const uint64_t aa = pack2(alpha, alpha);
 #pragma unroll
-        for (int h = 0; h < H; ++h) acc[r][h] = ffma2(acc[r][h], aa, 0ull);
+        for (int c = 0; c < H; ++c) acc[r][c] = ffma2(acc[r][c], aa, 0ull);
         mc2[r] = mc2n;
         mth[r] = sd + RESCALE_LOG2 / c2;
       }
@@ -71,7 +72,12 @@ __device__ __forceinline__ void dense_tile(
   }
 }
 
-template <int DP, int QPT, typename T>
+// SPLIT = 2: two lanes per query row, each over the keys of one parity; the
+// pair merges its two online-softmax states at the end (the larger reference
+// maximum, both normalisers and accumulators rescaled to it, the even lane's
+// state first in both lanes, so both hold the same values) and each lane
+// stores half the row.
+template <int DP, int QPT, typename T, int SPLIT = 1>
 __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
   constexpr int TK = dense_tile_keys<DP>();
   constexpr int H = DP / 2;  // column pairs
@@ -79,8 +85,9 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
   __shared__ __align__(16) float sk[2][TK * DP];
   __shared__ __align__(16) float sv[2][TK * DP];
 
+  constexpr int RPW = 32 * QPT / SPLIT;  // query rows per warp
   const int N = p.N, d = p.d;
-  const int groups = cdiv(N, 32 * QPT);
+  const int groups = cdiv(N, RPW);
   const int wpb = blockDim.x >> 5;
   const int cpe = cdiv(groups, wpb);
   const int b = blockIdx.x / cpe;
@@ -104,8 +111,9 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
   float mth[QPT];  // raw score above which the reference point moves
   float l[QPT];
 #pragma unroll
+  const int h = lane % SPLIT;
   for (int r = 0; r < QPT; ++r) {
-    qi[r] = g * 32 * QPT + r * 32 + lane;
+    qi[r] = g * RPW + r * (32 / SPLIT) + lane / SPLIT;
     float qr[DP];
     if (active && qi[r] < N) {
       load_row<DP, T>(qr, Q + (int64_t)qi[r] * p.st.qn, d, vec);
@@ -140,23 +148,57 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
     }
     __syncthreads();
     if (active)
-      dense_tile<DP, QPT>(sk[buf], sv[buf], min(TK, N - t0), t0, qi, qp, acc,
-                          mc2, mth, l, c2);
+      dense_tile<DP, QPT, SPLIT>(sk[buf], sv[buf], min(TK, N - t0), t0, qi,
+                                 qp, acc, mc2, mth, l, c2, h);
     __syncthreads();  // everyone is done with `buf` before it is refilled
   }
-  if (!active) return;
+  if (!active) return;  // warp-uniform: the shuffles below see all 32 lanes
+  if constexpr (SPLIT == 2) {
+#pragma unroll
+    for (int r = 0; r < QPT; ++r) {
+      const float mo = __shfl_xor_sync(0xffffffffu, mc2[r], 1);
+      const float lo = __shfl_xor_sync(0xffffffffu, l[r], 1);
+      uint64_t ao[H];
+#pragma unroll
+      for (int c = 0; c < H; ++c)
+        ao[c] = __shfl_xor_sync(0xffffffffu, acc[r][c], 1);
+      // (m0, l0, a0): the even lane's state, (m1, l1, a1): the odd lane's
+      const float m0 = h ? mo : mc2[r], m1 = h ? mc2[r] : mo;
+      const float l0 = h ? lo : l[r], l1 = h ? l[r] : lo;
+      const float m = fmaxf(m0, m1);
+      const float f0 = exp2f(m0 - m), f1 = exp2f(m1 - m);
+      l[r] = fmaf(l1, f1, l0 * f0);
+      const uint64_t ff0 = pack2(f0, f0), ff1 = pack2(f1, f1);
+#pragma unroll
+      for (int c = 0; c < H; ++c) {
+        const uint64_t a0 = h ? ao[c] : acc[r][c];
+        const uint64_t a1 = h ? acc[r][c] : ao[c];
+        acc[r][c] = ffma2(a1, ff1, ffma2(a0, ff0, 0ull));
+      }
+    }
+  }
 #pragma unroll
   for (int r = 0; r < QPT; ++r) {
     if (qi[r] >= N) continue;
     const float inv = 1.0f / l[r];
     float o[DP];
 #pragma unroll
-    for (int h = 0; h < H; ++h) {
-      const float2 f = unpack2(acc[r][h]);
-      o[2 * h] = f.x * inv;
-      o[2 * h + 1] = f.y * inv;
+    for (int c = 0; c < H; ++c) {
+      const float2 f = unpack2(acc[r][c]);
+      o[2 * c] = f.x * inv;
+      o[2 * c + 1] = f.y * inv;
     }
-    store_row<DP, T>(O + (int64_t)qi[r] * p.st.on, o, d, vec);
+    if constexpr (SPLIT == 1) {
+      store_row<DP, T>(O + (int64_t)qi[r] * p.st.on, o, d, vec);
+    } else {
+      // each lane of the pair stores half of the row's columns
+      float half[H];
+#pragma unroll
+      for (int c = 0; c < H; ++c) half[c] = h ? o[H + c] : o[c];
+      if (d > h * H)
+        store_row<H, T>(O + (int64_t)qi[r] * p.st.on + h * H, half, d - h * H,
+                        vec);
+    }
   }
 }
 
@@ -165,25 +207,28 @@ constexpr int dense_qpt() {
   return DP <= 16 ? 2 : 1;
 }
 
-template <int DP, int QPT, typename T>
+template <int DP, int QPT, typename T, int SPLIT = 1>
 static cudaError_t launch_dense_q(const AttnParams& p, cudaStream_t s) {
-  const int groups = cdiv(p.N, 32 * QPT);
+  const int groups = cdiv(p.N, 32 * QPT / SPLIT);
   const int wpb = groups < 4 ? groups : 4;
   const int cpe = cdiv(groups, wpb);
   const int64_t blocks = (int64_t)p.B * cpe;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  dense_kernel<DP, QPT, T><<<(unsigned)blocks, 32 * wpb, 0, s>>>(p);
+  dense_kernel<DP, QPT, T, SPLIT><<<(unsigned)blocks, 32 * wpb, 0, s>>>(p);
   return cudaGetLastError();
 }
 
-// One query row per lane for episodes under 128 agents: each episode then
-// spreads over up to four warps instead of one warp walking every key for
-// two rows per lane (the per-row arithmetic does not depend on QPT).
+// Short episodes at d <= 16 spread over up to four warps instead of one
+// warp walking every key for two rows per lane: up to 64 agents two lanes
+// per query row (each over half the keys), below 128 one lane per row (two
+// lanes per row measured slower there: N=100 36.5 -> 38.4 us at B=1024).
 template <int DP, typename T>
 static cudaError_t launch_dense_dp(const AttnParams& p, cudaStream_t s) {
   constexpr int QPT = dense_qpt<DP>();
-  if constexpr (QPT > 1)
-    if (p.N < 128) return launch_dense_q<DP, 1, T>(p, s);
+  if constexpr (QPT > 1) {
+    if (p.N <= 64) return launch_dense_q<DP, 1, T, 2>(p, s);
+    if (p.N < 128) return launch_dense_q<DP, 1, T, 1>(p, s);
+  }
   return launch_dense_q<DP, QPT, T>(p, s);
 }
 
