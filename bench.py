@@ -277,37 +277,45 @@ def _graph_us(fn, dev, stream, calls: int = 10, replays: int = 10):
 
 
 def _sweep_c5(ops, dev, stream) -> list:
-    """bf16 batch-scaling grid at B=4096 episodes on this GPU: dense and
-    top-k (k = 1, 2) through the tensor-core kernels. Informational rows
-    (inputs > L2 at N=512; 10 reps after one warm-up call)."""
+    """BASELINE configs[4], the bf16 batch-scaling grid on this GPU: B in
+    {256, 1024, 4096} episodes, N in {128, 512}, d in {16, 32, 64}, dense and
+    top-k (k = 1, 2) through the tensor-core kernels. Informational rows (10
+    reps after one warm-up call; inputs > L2 only at the largest sizes);
+    `*_dev_us` are the same calls replayed from a CUDA graph (device time,
+    which the API timing hides behind host cost at the smallest sizes)."""
     import torch
     peaks = _peaks()
     rows = []
-    B = 4096
-    for n_ in (128, 512):
-        for d_ in (16, 32, 64):
-            gs = torch.Generator().manual_seed(1234 + 7 * n_ + d_)
-            q_, k_, v_ = (torch.randn(B, n_, d_, generator=gs).to(torch.bfloat16).to(dev)
-                          for _ in range(3))
-            row = {"B": B, "N": n_, "d": d_}
-            reps = 10
-            ops.dense_attention(q_, k_, v_)
-            t = _time_loop(lambda s: ops.dense_attention(q_, k_, v_), reps, stream) / reps
-            flops = 4.0 * B * n_ * n_ * d_
-            byts = 4.0 * B * n_ * d_ * 2
-            row["dense_us"] = round(1e3 * t, 2)
-            row["dense_tflops"] = round(flops / (t * 1e-3) / 1e12, 1)
-            row["dense_frac_bf16_peak"] = round(flops / (t * 1e-3) / 1e12
-                                                / peaks["bf16_tflops"], 3)
-            row["dense_hbm_frac"] = round(byts / (t * 1e-3) / 1e9 / peaks["hbm_gbs"], 3)
-            for kk_ in (1, 2):
-                ops.topk_attention(q_, k_, v_, kk_)
-                t = _time_loop(lambda s: ops.topk_attention(q_, k_, v_, kk_), reps,
-                               stream) / reps
-                row[f"topk_k{kk_}_us"] = round(1e3 * t, 2)
-            row["agent_rows_per_s_topk_k2"] = B * n_ / (row["topk_k2_us"] * 1e-6)
-            rows.append(row)
-            del q_, k_, v_
+    grid = [(B, n_, d_) for B in (256, 1024, 4096) for n_ in (128, 512)
+            for d_ in (16, 32, 64)]
+    for B, n_, d_ in grid:
+        gs = torch.Generator().manual_seed(1234 + 7 * n_ + d_)
+        q_, k_, v_ = (torch.randn(B, n_, d_, generator=gs).to(torch.bfloat16).to(dev)
+                      for _ in range(3))
+        row = {"B": B, "N": n_, "d": d_}
+        reps = 10
+        ops.dense_attention(q_, k_, v_)
+        t = _time_loop(lambda s: ops.dense_attention(q_, k_, v_), reps, stream) / reps
+        row["dense_us"] = round(1e3 * t, 2)
+        row["dense_dev_us"], _ = _graph_us(
+            lambda s: ops.dense_attention(q_, k_, v_), dev, stream)
+        t_dev = (row["dense_dev_us"] or row["dense_us"]) * 1e-3
+        flops = 4.0 * B * n_ * n_ * d_
+        byts = 4.0 * B * n_ * d_ * 2
+        row["dense_tflops"] = round(flops / t_dev / 1e9, 1)
+        row["dense_frac_bf16_peak"] = round(flops / t_dev / 1e9 / peaks["bf16_tflops"], 3)
+        row["dense_hbm_frac"] = round(byts / t_dev / 1e6 / peaks["hbm_gbs"], 3)
+        for kk_ in (1, 2):
+            ops.topk_attention(q_, k_, v_, kk_)
+            t = _time_loop(lambda s: ops.topk_attention(q_, k_, v_, kk_), reps,
+                           stream) / reps
+            row[f"topk_k{kk_}_us"] = round(1e3 * t, 2)
+        row["topk_k2_dev_us"], _ = _graph_us(
+            lambda s: ops.topk_attention(q_, k_, v_, 2), dev, stream)
+        t2 = row["topk_k2_dev_us"] or row["topk_k2_us"]
+        row["agent_rows_per_s_topk_k2"] = B * n_ / (t2 * 1e-6)
+        rows.append(row)
+        del q_, k_, v_
     return rows
 
 
