@@ -1,6 +1,9 @@
-"""GPU parity: the short-episode top-k kernel (csrc/topk_small.cu: N < 128,
-d <= 16, k <= 8; one lane per query row, 4, 2 or 1 episodes per block) vs
-the CPU oracle, through the C ABI.
+"""GPU parity: the short-episode top-k kernel (csrc/topk_small.cu: d <= 16,
+k <= 8, episodes the tensor-core kernel does not take — up to 64 agents, up
+to 95 for k > 4, and up to 128 when d is not a multiple of 8 or rows are off
+the 16-byte grid; two lanes per query row up to 64 agents, else one) vs the
+CPU oracle, through the C ABI. Episodes of 65-127 agents in these tests that
+the tensor-core kernel takes check its part-filled tile as well.
 
 Bar as for every top-k kernel: retained indices equal to the oracle's on
 every row whose k-th and (k+1)-th scores are not within fp32 rounding of
@@ -45,10 +48,12 @@ def test_every_k_and_tie_rule(ops, k, mode, tie):
 
 
 @pytest.mark.parametrize("N,d,k", [(20, 7, 3), (60, 12, 2), (45, 1, 1),
-                                   (100, 8, 4), (9, 16, 8), (127, 5, 6)])
+                                   (100, 8, 4), (9, 16, 8), (127, 5, 6),
+                                   (80, 16, 6), (127, 12, 2), (90, 16, 8)])
 def test_widths_below_16(ops, N, d, k):
     """d < 16: columns past d are zero in shared memory; d not a multiple
-    of 4 takes the 4-byte path."""
+    of 4 takes the 4-byte path. (80, 16, 6), (90, 16, 8) and (127, 12, 2)
+    reach the one-lane-per-row form above 64 agents."""
     q, kt, v = qkv(12, N, d, seed=N * 3 + d)
     out, idx = ops.topk_attention(q, kt, v, k, return_indices=True)
     check_topk(q, kt, v, k, out, idx=idx)

@@ -1,9 +1,9 @@
 """GPU parity: fp32 top-k on the tensor cores (three exact bf16 planes per
 operand, six plane products per score) vs the CPU oracle.
 
-fp32 episodes of 128 or more agents with d a multiple of 8 up to 16, k <= 8
-and 16-byte aligned rows form their scores this way; other fp32 problems run
-the FFMA kernels. Same bar as every fp32 top-k kernel: retained indices
+fp32 episodes of 128 or more agents (from 65 for k <= 4, from 96 for k <= 8)
+with d a multiple of 8 up to 16, k <= 8 and 16-byte aligned rows form their
+scores this way; other fp32 problems run the FFMA kernels. Same bar as every fp32 top-k kernel: retained indices
 equal to the oracle's on every row whose k-th and (k+1)-th exact scores are
 not within fp32 rounding of each other (oracle.ambiguous_rows), outputs
 within rtol = atol = 1e-5.
@@ -170,3 +170,15 @@ def test_f32_tc_special_rows(ops):
     got = idx.long().cpu().numpy()
     np.testing.assert_array_equal(got[:, 5], np.tile([0, 1, 2], (4, 1)))
     check_topk(q, kt, v, 3, out, idx=idx)
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("N,k", [(65, 1), (65, 4), (72, 2), (95, 3), (96, 5),
+                                 (100, 8), (112, 2), (127, 4), (127, 7)])
+@pytest.mark.parametrize("mode,tie", [("argmax", "low"), ("sort", "high")])
+def test_part_filled_tile_below_128(ops, dtype, N, k, mode, tie):
+    """Episodes of 65-127 agents run one part-filled 128-row tile (k <= 4
+    from 65 agents, k <= 8 from 96): query rows and keys past N are masked."""
+    q, kt, v = qkv(20, N, 16, seed=3 * N + k, dtype=dtype)
+    out, idx = ops.topk_attention(q, kt, v, k, mode=mode, return_indices=True)
+    check_topk(q, kt, v, k, out, tie=tie, idx=idx)

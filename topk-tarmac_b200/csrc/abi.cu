@@ -54,22 +54,22 @@ bool topk_small_supported(const AttnParams& p);
 cudaError_t launch_topk_small(const AttnParams& p, int dtype, bool tie_high,
                               cudaStream_t s);
 
-// k <= 8 with the lowest- or highest-index tie rule: episodes under 128
-// agents with d <= 16 run one lane per query row (topk_small.cu); episodes
-// of 128 agents or more form their scores on the tensor cores (bf16
-// directly; fp32 as three exact bf16 planes, d a multiple of 8 up to 16,
-// 16-byte rows); otherwise the chunked FFMA kernel when the episode's keys
-// fit its shared memory, else the streaming kernel.
+// k <= 8 with the lowest- or highest-index tie rule: episodes of 128 agents
+// or more (from 65 for k <= 4, from 96 for k <= 8) form their scores on the
+// tensor cores (bf16 directly; fp32 as three exact bf16 planes, d a
+// multiple of 8 up to 16, 16-byte rows); other episodes up to 128 agents
+// with d <= 16 run one or two lanes per query row (topk_small.cu);
+// otherwise the chunked FFMA kernel when the episode's keys fit its shared
+// memory, else the streaming kernel.
 static cudaError_t launch_topk_small_k(const AttnParams& p, int dtype,
                                        bool tie_high, cudaStream_t s) {
-  // short episodes (N < 128): one lane per query row, several episodes per
-  // block (the tensor-core kernel needs N >= 128)
-  if (p.N < 128 && topk_small_supported(p))
-    return launch_topk_small(p, dtype, tie_high, s);
   if (dtype == TARMAC_BF16 && topk_tc_supported(p))
     return launch_topk_tc(p, tie_high, s);
   if (dtype == TARMAC_F32 && topk_tc_f32_supported(p))
     return launch_topk_tc_f32(p, tie_high, s);
+  // short episodes the tensor-core kernel does not take: one or two lanes
+  // per query row, several episodes per block
+  if (topk_small_supported(p)) return launch_topk_small(p, dtype, tie_high, s);
   if (chunk_fits(p.N, p.d, p.topk)) {
     if (dtype == TARMAC_BF16)
       return tie_high ? launch_topk_chunk_bf16_high(p, s)

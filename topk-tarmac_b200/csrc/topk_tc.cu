@@ -430,8 +430,17 @@ static bool a16(const void* x) {
 }
 
 // bf16, N >= 128, k <= 8: is the tensor-core top-k path available?
+// Episodes of 128 agents or more; below, from 65 agents for k <= 4 and from
+// 96 for k <= 8, where one part-filled 128-row tile measured faster than
+// the short-episode kernel (B=1024, d=16: N=96 k=2 15.2 vs 20.4 us fp32).
+// Both bounds leave more 8-key chunks per episode (at least 9) than the
+// chunk list holds.
+static bool tc_episode_ok(const AttnParams& p) {
+  return p.N >= 128 || (p.N >= 65 && (p.topk <= 4 || p.N >= 96));
+}
+
 bool topk_tc_supported(const AttnParams& p) {
-  return p.N >= 128 && p.d <= 128 && p.topk <= 8;
+  return tc_episode_ok(p) && p.d <= 128 && p.topk <= 8;
 }
 
 cudaError_t launch_topk_tc(const AttnParams& p, bool tie_high, cudaStream_t s) {
@@ -457,7 +466,7 @@ cudaError_t launch_topk_tc(const AttnParams& p, bool tie_high, cudaStream_t s) {
 // and O rows move as 16-byte pieces): is the split tensor-core path
 // available?
 bool topk_tc_f32_supported(const AttnParams& p) {
-  if (p.N < 128 || p.d > 16 || p.d % 8 != 0 || p.topk > 8) return false;
+  if (!tc_episode_ok(p) || p.d > 16 || p.d % 8 != 0 || p.topk > 8) return false;
   const Strides& t = p.st;
   return a16(p.q) && a16(p.k) && a16(p.v) && a16(p.o) && t.qn % 4 == 0 &&
          t.kn % 4 == 0 && t.vn % 4 == 0 && t.on % 4 == 0 && t.qb % 4 == 0 &&
