@@ -110,8 +110,8 @@ __global__ void __launch_bounds__(128) dense_kernel(AttnParams p) {
   float mc2[QPT];  // reference maximum times c2 (exponent units)
   float mth[QPT];  // raw score above which the reference point moves
   float l[QPT];
-#pragma unroll
   const int h = lane % SPLIT;
+#pragma unroll
   for (int r = 0; r < QPT; ++r) {
     qi[r] = g * RPW + r * (32 / SPLIT) + lane / SPLIT;
     float qr[DP];

@@ -1,5 +1,5 @@
 // topk_small.cu — fused top-k attention for short episodes on sm_100a:
-// N <= 128, d <= 16, k <= 8, one lane per query row.
+// N <= 128, d <= 16, k <= 8, one or two lanes per query row.
 //
 // Same function as topk_chunk_kernel and the tensor-core kernel (reference:
 // src/kernels/fused_topk_attention.py:211-289, streaming_topk_attention.py:
@@ -12,12 +12,12 @@
 //   query row (each scores every other key and keeps its own k best; the
 //   pair then merges the two buffers by shuffles and each lane stores half
 //   the row), and a block of four warps carries 4, 2 or 1 episodes. Above 64
-//   agents, four warps own one episode, one lane per row. The episode's warps copy its K
-//   and V rows into shared memory (16-byte cp.async for aligned fp32 rows,
-//   converted through registers otherwise; rows padded to DP + 4 floats)
-//   while each lane's Q row loads into registers.
-// * Each lane scores every key of its episode with dot_pairs (the key row is
-//   a broadcast read), the arithmetic of the chunked kernel's exact pass, so
+//   agents, four warps own one episode, one lane per row. The episode's
+//   warps copy its K and V rows into shared memory (16-byte cp.async for
+//   aligned fp32 rows, converted through registers otherwise; rows padded to
+//   DP + 4 floats) while each lane's Q row loads into registers.
+// * Each lane scores its keys with dot_pairs (the key rows are broadcast
+//   reads), the arithmetic of the chunked kernel's exact pass, so
 //   every score is bit-identical to it, and keeps the k best by (score,
 //   index) with the tie rule in a sorted register buffer. NaN scores are
 //   never retained (the chunked kernel's threshold test drops them too).
