@@ -23,12 +23,13 @@
  *   s[b,i,j] = (q[b,i,:] . k[b,j,:]) * scale, the diagonal j == i excluded;
  *   softmax over the retained peers of row i; out[b,i,:] = sum_j w_ij v[b,j,:].
  * Scores and accumulation are fp32. bf16 inputs with N >= 128 (top-k: from
- * N = 65 for k <= 4 and N = 96 for k <= 8) form their scores on the tensor
- * cores (exact bf16 products, fp32 accumulation; the dense path feeds its
- * softmax weights to P.V as bf16, as the reference's bf16 kernel does);
- * other bf16 inputs are widened to fp32 on load. fp32 top-k (k <= 8) and
- * dense inputs of those sizes with d a multiple of 8 up to 16 and 16-byte
- * aligned rows also run on the tensor cores: every operand (q,
+ * N = 65 for k <= 4 and N = 96 for k <= 8; dense: from N = 65) form their
+ * scores on the tensor cores (exact bf16 products, fp32 accumulation; the
+ * dense path feeds its softmax weights to P.V as bf16, as the reference's
+ * bf16 kernel does); other bf16 inputs are widened to fp32 on load. fp32
+ * top-k (k <= 8) inputs of those sizes and dense inputs from N = 96, with d
+ * a multiple of 8 up to 16 and 16-byte aligned rows, also run on the tensor
+ * cores: every operand (q,
  * k, v and the dense path's softmax weights) is split exactly into three
  * bf16 parts and six part products accumulate in fp32, an fp32-accurate
  * product (error within about 2^-23 * sum_c |a_c b_c| plus fp32

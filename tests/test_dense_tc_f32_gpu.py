@@ -1,6 +1,6 @@
 """GPU parity: fp32 dense attention on the tensor cores vs the CPU oracle.
 
-fp32 episodes of 128 or more agents with d in {8, 16} and 16-byte aligned
+fp32 episodes of 96 or more agents with d in {8, 16} and 16-byte aligned
 rows run Q K^T and P V on the tensor cores with every operand (Q, K, V and
 the softmax weights P) split exactly into three bf16 planes and six plane
 products per product, an fp32-accurate result; other fp32 shapes run the
@@ -100,3 +100,20 @@ def test_f32_dense_tc_zero_and_tiny_rows(ops):
     out = check(ops, q, k, v)
     vm = (v[:, :, :].sum(1) - v[:, 3]) / 255.0
     np.testing.assert_allclose(host(out[:, 3]), host(vm), rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("N,d,dtype", [(96, 16, torch.float32),
+                                       (100, 8, torch.float32),
+                                       (127, 16, torch.float32),
+                                       (65, 16, torch.bfloat16),
+                                       (100, 64, torch.bfloat16),
+                                       (127, 32, torch.bfloat16)])
+def test_dense_tc_part_filled_tile_below_128(ops, N, d, dtype):
+    """Dense episodes below 128 agents on one part-filled 128-row tile (bf16
+    from 65 agents, fp32 from 96): query rows and keys past N are masked."""
+    from _parity import tol_for
+    q, k, v = qkv(12, N, d, seed=5 * N + d, dtype=dtype)
+    out = ops.dense_attention(q, k, v)
+    assert out.dtype == dtype
+    ref = oracle.dense_attention(host(q), host(k), host(v))
+    np.testing.assert_allclose(host(out), ref, **tol_for(dtype))
