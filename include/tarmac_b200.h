@@ -135,7 +135,7 @@ int tarmac_streaming_topk_attention(const void *q, const void *k,
  * naming an index outside [0, N) is written as NaN (no out-of-bounds read).
  * Replaces fused_prescore_attention and _fused_prescore_kernel
  * (src/kernels/fused_prescore_attention.py:27-114) and the eager
- * prescore_attention (src/kernels/prescore_selection.py:442-453). */
+ * prescore_attention (src/kernels/prescore_selection.py:184-195). */
 int tarmac_prescore_attention(const void *q, const void *k, const void *v,
                               void *out, const int64_t *strides,
                               const void *idx, int idx_is_i64, int kk, int B,
@@ -146,14 +146,14 @@ int tarmac_prescore_attention(const void *q, const void *k, const void *v,
 /* pos: fp32 [B, N, 2] contiguous positions. Per episode: min/max normalise,
  * quantise to `bits` per axis (truncation, clamp), interleave x bits at even
  * and y bits at odd positions. code_out: int64 [B, N].
- * Replaces _morton_code (src/kernels/prescore_selection.py:313-326). */
+ * Replaces _morton_code (src/kernels/prescore_selection.py:51-68). */
 int tarmac_morton_code(const float *pos, int B, int N, int bits,
                        int64_t *code_out, void *stream);
 
 /* Codes as above, stable ascending sort per episode (ties by agent index),
  * then for agent at rank r the peers at ranks r+1..r+h and r-1..r-(k-h)
  * modulo N, h = (k+1)/2. idx_out: int64 [B, N, k]. N <= 4096, 1 <= k <= N-1.
- * Replaces select_morton_window (src/kernels/prescore_selection.py:329-342),
+ * Replaces select_morton_window (src/kernels/prescore_selection.py:71-84),
  * with the bit width as a parameter (the reference fixes 10). */
 int tarmac_morton_select(const float *pos, int B, int N, int k, int bits,
                          int64_t *idx_out, void *stream);
@@ -163,7 +163,7 @@ int tarmac_morton_select(const float *pos, int B, int N, int k, int bits,
  * tarmac_prescore_attention, one kernel, no index tensor written unless
  * idx_out (int64 [B, N, k], optional) is given. N <= 4096.
  * Replaces prescore_full(q, k, v, pos, kk, "morton_window")
- * (src/kernels/prescore_selection.py:456-458). */
+ * (src/kernels/prescore_selection.py:198-200). */
 int tarmac_morton_prescore_attention(const void *q, const void *k,
                                      const void *v, void *out,
                                      const int64_t *strides, const float *pos,
@@ -189,7 +189,7 @@ int tarmac_knn_select(const float *pos, int B, int N, int k, int64_t *idx_out,
  * selector runs instead, as in the reference; an agent whose runs hold fewer
  * than k candidates takes its exact k nearest. Same layout and limits as
  * tarmac_knn_select. Replaces select_grid_knn
- * (src/kernels/prescore_selection.py:81-162). */
+ * (src/kernels/prescore_selection.py:87-164). */
 int tarmac_grid_knn_select(const float *pos, int B, int N, int k,
                            int64_t *idx_out, void *stream);
 
@@ -274,9 +274,12 @@ int tarmac_dense_attention_backward(const void *q, const void *k,
  * of the library image, so every GPU that loads the library holds it until
  * the process exits.
  * Limit: B * N <= 524288 query rows (TARMAC_ERR_SCRATCH beyond).
- * The first call on a device looks up the array's device address on that
- * device (the device current at the call, which must be the device of the
- * pointers); make that first call before any stream capture. Every call
+ * The array's device address belongs to a CUDA context: the first call in
+ * each context (the context current at the call, which must own the
+ * pointers) looks the address up and caches it under that context's id, so
+ * a context created after cudaDeviceReset, or one the caller made current
+ * through the driver API, gets its own lookup. Make the first call in a
+ * context before any stream capture in it. Every call
  * shares the one array: calls that overlap on the GPU (other streams, other
  * threads) race on it, so serialise them. No scratch contents need to start
  * at zero (each call writes the statistics before reading them).

@@ -193,7 +193,7 @@ def dense_attention(q, k, v):
 def prescore_attention(q, k, v, idx):
     """Attention over the given peers idx [B, N, kk].
 
-    prescore_attention (src/kernels/prescore_selection.py:442-453): gather the
+    prescore_attention (src/kernels/prescore_selection.py:184-195): gather the
     kk key and value rows, scores q.k_j / sqrt(d), softmax over the kk, sum.
     float64 arithmetic. Rows naming a peer outside [0, N) are NaN.
     """
@@ -222,7 +222,7 @@ def gather_attention_grad(q, k, v, idx, g, scale: float | None = None):
 
     The eager path gathers the selected rows and contracts
     (src/agents/mappo.py:211-222 topk_gather, 279-286 zorder_k;
-    prescore_selection.py:442-453): s = q.k_j * scale, w = softmax(s),
+    prescore_selection.py:184-195): s = q.k_j * scale, w = softmax(s),
     out = sum w v_j. The indices come from topk / the Morton selector and
     carry no gradient, so autograd's result is the chain rule through
     gather, softmax and the two contractions, with scatter-adds into dk, dv.
@@ -324,7 +324,7 @@ def knn_ambiguous(pos: np.ndarray, k: int, tol: float = 1e-6) -> np.ndarray:
 
 
 def grid_knn_shape(N: int, k: int) -> tuple[int, int]:
-    """Grid side and per-cell capacity (prescore_selection.py:81-97)."""
+    """Grid side and per-cell capacity (prescore_selection.py:87-101)."""
     occ = max(2, k)
     G = max(1, int((N / occ) ** 0.5))
     mean = N / (G * G)
@@ -334,7 +334,7 @@ def grid_knn_shape(N: int, k: int) -> tuple[int, int]:
 def grid_knn(pos: np.ndarray, k: int) -> np.ndarray:
     """Grid kNN, int64 [B, N, k] by increasing (distance, index).
 
-    select_grid_knn (src/kernels/prescore_selection.py:103-162): cells of a
+    select_grid_knn (src/kernels/prescore_selection.py:107-164): cells of a
     G x G grid over the episode's bounding box (normalise, scale by G,
     truncate, clamp), agents sorted by cell id x*G + y (stably: equal cells
     keep agent order), and for each agent the three sorted runs from cell
@@ -419,7 +419,7 @@ _SPREAD = ((8, 0x00FF00FF), (4, 0x0F0F0F0F), (2, 0x33333333), (1, 0x55555555))
 
 def _spread_bits(x: np.ndarray) -> np.ndarray:
     """Insert a zero between consecutive bits of a value below 2^16
-    (prescore_selection.py:313-317; its first (16, 0x0000FFFF) step is the
+    (prescore_selection.py:51-59; its first (16, 0x0000FFFF) step is the
     identity for such values)."""
     x = x.astype(np.int64)
     for sh, mask in _SPREAD:
@@ -428,7 +428,7 @@ def _spread_bits(x: np.ndarray) -> np.ndarray:
 
 
 def morton_code(pos: np.ndarray, bits: int = 10) -> np.ndarray:
-    """int64 [B, N] Morton codes (prescore_selection.py:320-326).
+    """int64 [B, N] Morton codes (prescore_selection.py:62-68).
 
     Per episode and axis: lo/hi = min/max, span = max(hi - lo, 1e-6),
     g = trunc((pos - lo) / span * (2^bits - 1)) clamped to [0, 2^bits - 1],
@@ -445,12 +445,12 @@ def morton_code(pos: np.ndarray, bits: int = 10) -> np.ndarray:
 
 
 def morton_window(pos: np.ndarray, k: int, bits: int = 10) -> np.ndarray:
-    """int64 [B, N, k] Z-order window peers (prescore_selection.py:329-342).
+    """int64 [B, N, k] Z-order window peers (prescore_selection.py:71-84).
 
     Agents sorted by code (stable: equal codes keep index order); the agent at
     rank r keeps the agents at ranks r+1..r+h and r-1..r-(k-h), modulo N,
     h = (k+1)//2, in that order. The reference sorts with an unstable argsort
-    (line 333); the stable order is the deterministic member of its outcomes.
+    (line 75); the stable order is the deterministic member of its outcomes.
     """
     code = morton_code(pos, bits)
     B, N = code.shape

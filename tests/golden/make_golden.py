@@ -6,10 +6,10 @@ on the CPU, and stores inputs and outputs as ``tests/golden/*.npz``:
 * the reference's eager functions: ``reference_topk_attention``
   (src/kernels/fused_topk_attention.py:390-402), ``dense_unfused``
   (scripts/bench_attention_core.py:74-75), ``_morton_code`` and
-  ``select_morton_window`` (src/kernels/prescore_selection.py:320-342),
-  ``prescore_attention`` (src/kernels/prescore_selection.py:442-453),
+  ``select_morton_window`` (src/kernels/prescore_selection.py:51-84),
+  ``prescore_attention`` (src/kernels/prescore_selection.py:184-195),
   ``select_radius_knn``, ``select_grid_knn``, ``grid_knn_recall``
-  (src/kernels/prescore_selection.py:35-170);
+  (src/kernels/prescore_selection.py:35-172);
 * the reference's Triton kernels run by Triton's CPU interpreter
   (``TRITON_INTERPRET=1``), which pin the kernel-specific tie rules:
   ``fused_topk_attention_tiled`` (lowest index), ``fused_topk_attention_sort``

@@ -69,15 +69,38 @@ def test_cpu_tensors_fail_loudly():
         ps.select_morton_window(torch.zeros(2, 8, 2), 2)
 
 
-def test_selectors_need_cuda_and_ledger_is_out_of_scope():
+def test_selectors_need_cuda_and_ledger_needs_reference_tree():
     pos = torch.zeros(1, 8, 2)
     for fn in (ps.select_radius_knn, ps.select_grid_knn, ps.grid_knn_recall):
         with pytest.raises(RuntimeError, match="CUDA"):
             fn(pos, 2)
+    # outside the reference tree there is no src.analysis package
     with pytest.raises(NotImplementedError):
         ps.analytic_flops("morton_window", 1, 8, 16, 2)
     assert ps.grid_knn_shape(512, 2) == (16, 8)
     assert ps.grid_knn_shape(600, 2) == oracle.grid_knn_shape(600, 2)
+
+
+def test_analytic_flops_delegates_to_the_reference_ledger(monkeypatch):
+    """Inside the reference tree, analytic_flops returns partial_counts'
+    result unchanged (prescore_selection.py:203-212)."""
+    import sys
+    import types
+    seen = {}
+
+    def partial_counts(selector, B, N, d, kk):
+        seen["args"] = (selector, B, N, d, kk)
+        return {"selector": 1, "count_model": "stub"}
+
+    pkg = types.ModuleType("src.analysis")
+    mod = types.ModuleType("src.analysis.selector_costs")
+    mod.partial_counts = partial_counts
+    pkg.selector_costs = mod
+    monkeypatch.setitem(sys.modules, "src.analysis", pkg)
+    monkeypatch.setitem(sys.modules, "src.analysis.selector_costs", mod)
+    got = ps.analytic_flops("grid_knn", 4, 64, 16, 2)
+    assert got == {"selector": 1, "count_model": "stub"}
+    assert seen["args"] == ("grid_knn", 4, 64, 16, 2)
 
 
 def test_tuned_cfg_absent_table_is_none():

@@ -59,6 +59,23 @@ def test_widths_below_16(ops, N, d, k):
     check_topk(q, kt, v, k, out, idx=idx)
 
 
+@pytest.mark.parametrize("N,d,k", [(128, 12, 3), (128, 5, 8), (128, 1, 1),
+                                   (128, 16, 2)])
+@pytest.mark.parametrize("mode,tie", [("argmax", "low"), ("sort", "high")])
+def test_full_128_agent_episode(ops, N, d, k, mode, tie):
+    """N = 128, the kernel's largest episode (four warps, one lane per row,
+    every lane of the block busy): widths the tensor-core kernel declines
+    (d not a multiple of 8), and d = 16 reached through a row stride off the
+    16-byte grid, under both tie rules."""
+    if d == 16:
+        base = qkv(10, N, d + 1, seed=N + d + k)
+        q, kt, v = (x[..., :d] for x in base)        # row stride 17 floats
+    else:
+        q, kt, v = qkv(10, N, d, seed=N + d + k)
+    out, idx = ops.topk_attention(q, kt, v, k, mode=mode, return_indices=True)
+    check_topk(q, kt, v, k, out, tie=tie, idx=idx)
+
+
 @pytest.mark.parametrize("N,k", [(32, 1), (64, 2), (100, 4), (48, 8)])
 def test_bf16(ops, N, k):
     q, kt, v = qkv(24, N, 16, seed=N + k, dtype=torch.bfloat16)

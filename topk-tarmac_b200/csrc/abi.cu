@@ -17,22 +17,29 @@
 namespace tarmac {
 
 cudaError_t raise_smem_limit(const void* fn, size_t bytes) {
-  constexpr int MAX_DEV = 64;
+  struct Key {
+    const void* fn;
+    unsigned long long ctx;
+    bool operator==(const Key& o) const { return fn == o.fn && ctx == o.ctx; }
+  };
+  struct KeyHash {
+    size_t operator()(const Key& k) const {
+      return std::hash<const void*>()(k.fn) ^ (size_t)(k.ctx * 0x9E3779B97F4A7C15ull);
+    }
+  };
   static std::mutex mu;
-  static std::unordered_map<const void*, std::array<size_t, MAX_DEV>> done;
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
+  static std::unordered_map<Key, size_t, KeyHash> done;
+  unsigned long long ctx = 0;
+  // without a readable context id the attribute is set on every call
+  const bool keyed = current_context_id(&ctx);
   std::lock_guard<std::mutex> lock(mu);
-  auto it = done.find(fn);
-  if (it == done.end()) {
-    std::array<size_t, MAX_DEV> zero{};
-    it = done.emplace(fn, zero).first;
+  if (keyed) {
+    auto it = done.find(Key{fn, ctx});
+    if (it != done.end() && it->second >= bytes) return cudaSuccess;
   }
-  if (dev >= 0 && dev < MAX_DEV && it->second[dev] >= bytes) return cudaSuccess;
-  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)bytes);
-  if (e == cudaSuccess && dev >= 0 && dev < MAX_DEV) it->second[dev] = bytes;
+  cudaError_t e = cudaFuncSetAttribute(
+      fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e == cudaSuccess && keyed) done[Key{fn, ctx}] = bytes;
   return e;
 }
 

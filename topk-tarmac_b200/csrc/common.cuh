@@ -37,12 +37,19 @@ struct AttnParams {
 
 __host__ __device__ constexpr int cdiv(int a, int b) { return (a + b - 1) / b; }
 
-// Raise kernel `fn`'s dynamic shared-memory limit to at least `bytes` on the
-// current device. The attribute lasts for the process, so it is set only
-// when this process has not yet set that much for this kernel and device (a
-// cudaFuncSetAttribute on every launch costs host time that small problems
-// notice). Safe from several host threads (abi.cu).
+// Raise kernel `fn`'s dynamic shared-memory limit to at least `bytes` in the
+// current CUDA context. The attribute lasts as long as the context, so it is
+// set only when this process has not yet set that much for this kernel in
+// this context (a cudaFuncSetAttribute on every launch costs host time that
+// small problems notice); a new context (after cudaDeviceReset, or one the
+// caller made current through the driver API) sets it again. Safe from
+// several host threads (abi.cu).
 cudaError_t raise_smem_limit(const void* fn, size_t bytes);
+
+// Process-unique id of the calling thread's current CUDA context (the
+// driver's cuCtxGetId); false when no context is current or the driver does
+// not offer the call (noalloc.cu).
+bool current_context_id(unsigned long long* id);
 
 // ---------------------------------------------------------------------------
 // element conversion

@@ -1,7 +1,7 @@
 // morton.cu — Z-order (Morton) peer selection and the fused select-before-
 // scoring kernel on sm_100a.
 //
-// Restates src/kernels/prescore_selection.py:313-342:
+// Restates src/kernels/prescore_selection.py:51-84:
 //   _morton_code: per-episode min/max normalise, quantise to `bits` per axis
 //     ((pos - lo) / span * (2^bits - 1), truncated, clamped), interleave;
 //   select_morton_window: argsort of the codes, rank, and the peers at ranks

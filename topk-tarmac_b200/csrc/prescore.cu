@@ -4,7 +4,7 @@
 // 27-81): for each query row, walk its kk given peers in order, score each
 // (q . k_j * scale), keep an online softmax (running max, normaliser,
 // accumulator) and write only the result. The eager counterpart is
-// prescore_attention (src/kernels/prescore_selection.py:442-453).
+// prescore_attention (src/kernels/prescore_selection.py:184-195).
 //
 // Layout: d <= 16: one thread per query row (its softmax runs once). For
 // N <= 512 with 16-byte rows, one block per episode stages the episode's K
