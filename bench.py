@@ -16,8 +16,9 @@ around the timed region, elapsed time = max over ranks.
 is the same metric through the reference-facing call
 (src.kernels.fused_topk_attention.fused_topk_attention_tiled) with pinned
 host buffers and the host<->device copies inside the timed region.
-``--impl reference`` times the CPU port of the reference's eager path
-(oracle/, fp32) on the host cores instead.
+``--impl reference`` times the reference's eager PyTorch path on the host
+cores instead (oracle/eager_torch.py: the same ATen calls, fp32, all host
+threads), as does the ``cpu_baseline`` leg of the default run.
 """
 
 from __future__ import annotations
@@ -46,17 +47,6 @@ REF_PUBLISHED_US = 837.7
 
 def log(*a) -> None:
     print(*a, file=sys.stderr, flush=True)
-
-
-def _profiled_traffic() -> float | None:
-    """DRAM bytes (read + write) of one top-k launch at this workload, from the
-    committed ncu summary (line ``traffic_bytes_per_launch: N``)."""
-    f = REPO / "profiles" / "topk_tc_f32_c2.md"
-    if not f.exists():
-        return None
-    import re
-    m = re.search(r"traffic_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
-    return float(m.group(1)) if m else None
 
 
 def _peaks() -> dict:
@@ -139,70 +129,99 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# the reference arm: the CPU port of the reference's eager path
+# the reference arm: the reference's eager PyTorch path on the host cores
 # ---------------------------------------------------------------------------
 
 def _cpu_threads() -> int:
+    """Host threads this process may run on; torch's intra-op pool is set to
+    that many (the reference's CPU protocol, microbenchmark_comm.py:236-264)."""
     try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 1) for i in threadpool_info()
-             if i.get("user_api") == "blas"]
-        if n:
-            return int(max(n))
-    except Exception:
-        pass
-    return os.cpu_count() or 1
-
-
-def cpu_baseline(episodes: int, budget_s: float, reps_min: int = 1) -> dict:
-    """Time oracle.topk_attention(exact=False) — the reference's eager fp32
-    algorithm restated in numpy — on a sample of ``episodes`` episodes of the
-    workload, repeated for about ``budget_s`` seconds; best rate wins."""
-    import numpy as np
+        n = len(os.sched_getaffinity(0))
+    except AttributeError:
+        n = os.cpu_count() or 1
     import torch
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
 
-    import oracle
-    g = torch.Generator().manual_seed(SEED)
-    q, k, v = (torch.randn(episodes, N_AGENTS, HEAD_D, generator=g).numpy()
-               for _ in range(3))
-    oracle.topk_attention(q[:1], k[:1], v[:1], TOPK, exact=False, want_mask=False)
+
+_PORT_NOTE = ("the reference's eager PyTorch path restated op for op "
+              "(oracle/eager_torch.py: same ATen calls on the same shapes, "
+              "outputs bit-identical to the reference's functions)")
+
+
+def _cpu_inputs(episodes: int, N: int, d: int, seed: int, pos: bool = False):
+    import torch
+    g = torch.Generator().manual_seed(seed)
+    t = [torch.randn(episodes, N, d, generator=g) for _ in range(3)]
+    if pos:
+        t.append(torch.rand(episodes, N, 2, generator=g))
+    return t
+
+
+def _cpu_rate(fn, rows: int, budget_s: float, reps_min: int = 2):
+    """Best agent-rows/s of fn() over about budget_s seconds (min time,
+    after one warm-up call), and the repetition count."""
+    fn()
     times = []
     t_end = time.perf_counter() + budget_s
     while len(times) < reps_min or time.perf_counter() < t_end:
         t0 = time.perf_counter()
-        oracle.topk_attention(q, k, v, TOPK, exact=False, want_mask=False)
+        fn()
         times.append(time.perf_counter() - t0)
-    best = min(times)
-    return {"value": episodes * N_AGENTS / best, "unit": "agent-rows/s",
-            "cores": _cpu_threads(), "kind": "port",
+    return rows / min(times), len(times), min(times)
+
+
+def cpu_baseline(episodes: int, budget_s: float) -> dict:
+    """The reference's eager CPU path on this host's cores, on a sample of
+    ``episodes`` episodes of each workload: the headline top-k (C2 N=512
+    k=2), dense (dense_unfused) at the same shape, and select-before-scoring
+    (C4 N=512 k=2, 16-bit Morton window + prescore attention). Each leg runs
+    for about budget_s / 3 seconds; the best repetition counts."""
+    from oracle import eager_torch as et
+    cores = _cpu_threads()
+    rows = episodes * N_AGENTS
+    q, k, v = _cpu_inputs(episodes, N_AGENTS, HEAD_D, SEED)
+    top, reps, best = _cpu_rate(lambda: et.topk_gather(q, k, v, TOPK), rows,
+                                budget_s / 3)
+    dense, _, _ = _cpu_rate(lambda: et.dense(q, k, v), rows, budget_s / 3)
+    q4, k4, v4, p4 = _cpu_inputs(episodes, 512, 16, 4242 + 512, pos=True)
+    zord, _, _ = _cpu_rate(
+        lambda: et.prescore(q4, k4, v4, et.morton_window(p4, 2, 16)),
+        episodes * 512, budget_s / 3)
+    return {"value": top, "unit": "agent-rows/s", "cores": cores,
+            "kind": "port",
             "sample": (f"{episodes} episodes of B={B_PER_GPU} N={N_AGENTS} "
-                       f"d={HEAD_D} k={TOPK} fp32, best of {len(times)} "
-                       f"repetitions (numpy port of the reference's eager "
-                       f"top-k path, oracle/tarmac_oracle.py)"),
-            "seconds_per_sample": best}
+                       f"d={HEAD_D} k={TOPK} fp32, best of {reps} repetitions; "
+                       + _PORT_NOTE),
+            "seconds_per_sample": best,
+            "dense_agent_rows_per_s": dense,
+            "zorder_c4_agent_rows_per_s": zord,
+            "zorder_sample": (f"{episodes} episodes of C4 N=512 k=2, 16-bit "
+                              "Morton window + prescore attention, fp32")}
 
 
 def run_reference(args) -> int:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
-    # size each step so the whole --warmup/--steps run stays near a minute
-    cal = cpu_baseline(1, 0.0)
-    per_ep = cal["seconds_per_sample"]
+    # the reference's eager top-k path on all host threads; each step is a
+    # sample of the workload sized so the whole --warmup/--steps run stays
+    # near a minute
+    from oracle import eager_torch as et
+    cores = _cpu_threads()
+    q1, k1, v1 = _cpu_inputs(1, N_AGENTS, HEAD_D, SEED)
+    et.topk_gather(q1, k1, v1, TOPK)
+    t0 = time.perf_counter()
+    et.topk_gather(q1, k1, v1, TOPK)
+    per_ep = max(time.perf_counter() - t0, 1e-4)
     total = max(1, args.steps + args.warmup)
-    eps = int(max(1, min(64, 60.0 / (total * per_ep))))
-    import numpy as np
-    import torch
-
-    import oracle
-    g = torch.Generator().manual_seed(SEED)
-    q, k, v = (torch.randn(eps, N_AGENTS, HEAD_D, generator=g).numpy()
-               for _ in range(3))
+    eps = int(max(1, min(B_PER_GPU, 60.0 / (total * per_ep))))
+    q, k, v = _cpu_inputs(eps, N_AGENTS, HEAD_D, SEED)
     for _ in range(args.warmup):
-        oracle.topk_attention(q, k, v, TOPK, exact=False, want_mask=False)
+        et.topk_gather(q, k, v, TOPK)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.topk_attention(q, k, v, TOPK, exact=False, want_mask=False)
+        et.topk_gather(q, k, v, TOPK)
     el = time.perf_counter() - t0
     rate = eps * N_AGENTS * args.steps / el
     line = {
@@ -213,9 +232,10 @@ def run_reference(args) -> int:
         "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic", "config": _config(args.gpus),
         "cpu_baseline": {"value": rate, "unit": "agent-rows/s",
-                         "cores": _cpu_threads(), "kind": "port",
-                         "sample": f"{eps} episodes per step (of B={B_PER_GPU}"
-                                   f" N={N_AGENTS} d={HEAD_D} k={TOPK})"},
+                         "cores": cores, "kind": "port",
+                         "sample": (f"{eps} episodes per step (of B={B_PER_GPU}"
+                                    f" N={N_AGENTS} d={HEAD_D} k={TOPK}); "
+                                    + _PORT_NOTE)},
         "e2e": {"value": rate, "unit": "agent-rows/s",
                 "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -583,7 +603,9 @@ def run_ours(args) -> int:
     # -- sweep of the C2 grid (informational, warm L2) -----------------------
     sweep = []
     if rank == 0 and not args.no_sweep:
-        for n_ in (32, 64, 128, 256, 384, 512):
+        # configs[1]'s N grid, extended to 768 and 1024 so the fp32 top-k /
+        # dense ratio covers every N from 64 to 1024 at one batch size
+        for n_ in (32, 64, 128, 256, 384, 512, 768, 1024):
             gs = torch.Generator().manual_seed(1234 + 7 * n_ + d)
             q_, k_, v_ = (torch.randn(B, n_, d, generator=gs).to(dev) for _ in range(3))
             reps = 30
@@ -613,6 +635,17 @@ def run_ours(args) -> int:
                 lambda s: ops.dense_attention(q_, k_, v_), dev, stream)
             sweep.append(row)
         del q_, k_, v_
+    # fused top-k (k = 1, 2) over our own dense kernel, fp32, B=1024, device
+    # time from CUDA graph replays: the target is < 1 at every N in 64..1024
+    ratio_by_n = {}
+    for row in sweep:
+        if row["N"] < 64 or not row.get("dense_dev_us"):
+            continue
+        for kk_ in (1, 2):
+            t = row.get(f"topk_k{kk_}_dev_us")
+            if t:
+                ratio_by_n.setdefault(f"k{kk_}", {})[str(row["N"])] = round(
+                    t / row["dense_dev_us"], 3)
     sweep_c5 = _sweep_c5(ops, dev, stream) if rank == 0 and not args.no_sweep else []
     sweep_c3 = _sweep_c3(ops, dev, stream) if rank == 0 and not args.no_sweep else []
     sweep_c4 = _sweep_c4(ops, dev, stream) if rank == 0 and not args.no_sweep else []
@@ -654,24 +687,37 @@ def run_ours(args) -> int:
                 "h2d_bytes_per_step": 3 * B * N * d * 4,
                 "d2h_bytes_per_step": B * N * d * 4,
                 "us_per_step": 1e3 * ems},
-        "roofline": {"bound": "hbm", "achieved": achieved_gbs,
-                     "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved_gbs / peaks["hbm_gbs"],
-                     "traffic": (args.traffic if args.traffic is not None
-                                 else _profiled_traffic()),
-                     "peak_src": peaks["src"]},
-        "roofline_compute": {"bound": "tensor", "achieved": achieved_tc,
-                             "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                             "frac": achieved_tc / peaks["bf16_tflops"],
-                             "flops_per_launch": tc_flops,
-                             "note": "bf16 tensor flops executed: six plane "
-                                     "products (exact hi/mid/lo split of the "
-                                     "fp32 q and k) per score",
-                             "peak_src": f"{peaks['src']}: bf16 GEMM burst",
-                             "fp32_equivalent_tflops": achieved_tf,
-                             "fp32_simt_gemm_tflops": fp32_tf,
-                             "fp32_simt_src": "measured: cuBLAS fp32 GEMM "
-                                              "8192^3, TF32 off, this run"},
+        # The kernel's compute roof is the tensor pipe (every fp32 score is
+        # six exact bf16 plane products); HBM is far from binding (AI of the
+        # fp32 top-k is N/8 flop/B). What binds in practice is the issue rate
+        # of the selection scan (ALU), which no roof here measures.
+        "roofline": {"bound": "tensor", "achieved": achieved_tc,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved_tc / peaks["bf16_tflops"],
+                     "flops_per_launch": tc_flops,
+                     "traffic": args.traffic,
+                     "traffic_note": ("ncu dram bytes of one launch, given "
+                                      "with --traffic" if args.traffic
+                                      else "not measured in this run"),
+                     "peak_src": f"{peaks['src']}: bf16 GEMM burst",
+                     "note": "bf16 tensor flops the kernel executes: six "
+                             "plane products (exact hi/mid/lo split of the "
+                             "fp32 q and k) per score",
+                     "binding": "ALU issue of the selection scan"},
+        "roofline_hbm": {"bound": "hbm", "achieved": achieved_gbs,
+                         "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                         "frac": achieved_gbs / peaks["hbm_gbs"],
+                         "bytes_per_launch": alg_bytes,
+                         "peak_src": peaks["src"]},
+        "roofline_fp32": {"achieved": achieved_tf, "unit": "TFLOP/s",
+                          "flops_per_launch": alg_flops,
+                          "fp32_simt_gemm_tflops": fp32_tf,
+                          "frac_of_fp32_simt_gemm": (achieved_tf / fp32_tf
+                                                     if fp32_tf else None),
+                          "note": "algorithmic flops (2BN^2d + 2BNkd) against "
+                                  "a cuBLAS fp32 GEMM with TF32 off, measured "
+                                  "in this run (the FFMA roof)"},
+        "topk_over_dense_by_N": ratio_by_n,
         "clocks": clk.summary(),
         "sweep_c2_us": sweep,
         "sweep_c5_bf16": sweep_c5,
@@ -695,7 +741,7 @@ def main() -> int:
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--cpu-episodes", type=int, default=16)
+    ap.add_argument("--cpu-episodes", type=int, default=64)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--traffic", type=float, default=None,
                     help="ncu dram bytes per launch of the top-k kernel")
