@@ -60,16 +60,25 @@ cudaError_t launch_topk_tc_f32(const AttnParams& p, bool tie_high,
 bool topk_small_supported(const AttnParams& p);
 cudaError_t launch_topk_small(const AttnParams& p, int dtype, bool tie_high,
                               cudaStream_t s);
+bool topk_ws_supported(const AttnParams& p, int dtype);
+cudaError_t launch_topk_ws(const AttnParams& p, int dtype, bool tie_high,
+                           cudaStream_t s);
 
 // k <= 8 with the lowest- or highest-index tie rule: episodes of 128 agents
 // or more (from 65 for k <= 4, from 96 for k <= 8) form their scores on the
 // tensor cores (bf16 directly; fp32 as three exact bf16 planes, d a
-// multiple of 8 up to 16, 16-byte rows); other episodes up to 128 agents
-// with d <= 16 run one or two lanes per query row (topk_small.cu);
-// otherwise the chunked FFMA kernel when the episode's keys fit its shared
-// memory, else the streaming kernel.
+// multiple of 8 up to 16, 16-byte rows) — large batches of 385-512-agent
+// episodes in the persistent warp-specialized kernel (topk_ws.cu) where it
+// measured faster, others one 128-query block at a time (topk_tc.cu); both
+// return the same bits. Other episodes up to 128 agents with d <= 16 run
+// one or two lanes per query row (topk_small.cu); otherwise the chunked
+// FFMA kernel when the episode's keys fit its shared memory, else the
+// streaming kernel.
 static cudaError_t launch_topk_small_k(const AttnParams& p, int dtype,
                                        bool tie_high, cudaStream_t s) {
+  if (topk_ws_supported(p, dtype) &&
+      (dtype == TARMAC_BF16 ? topk_tc_supported(p) : topk_tc_f32_supported(p)))
+    return launch_topk_ws(p, dtype, tie_high, s);
   if (dtype == TARMAC_BF16 && topk_tc_supported(p))
     return launch_topk_tc(p, tie_high, s);
   if (dtype == TARMAC_F32 && topk_tc_f32_supported(p))
