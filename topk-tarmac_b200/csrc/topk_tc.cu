@@ -69,11 +69,10 @@ __host__ __device__ constexpr int tc_planes(bool f32) { return f32 ? 3 : 1; }
 // dtypes (32, 16 and 4 were slower).
 __host__ __device__ constexpr int tc_chunk(int, bool) { return 8; }
 
-// A chunk-list entry packs the chunk id and the shared-memory slot holding
-// its saved scores as (id << 3) | slot; an empty entry has id -1, so it is
-// negative and sorts last as an unsigned value.
-__device__ __forceinline__ int entry_id(int e) { return e >> 3; }
-__device__ __forceinline__ int entry_slot(int e) { return e & 7; }
+// A chunk-list entry packs the chunk id and the byte offset of the
+// shared-memory slot holding its saved scores as (id << 8) | (slot * CH * 4);
+// an empty entry has id -1, so it is negative and sorts last as an unsigned
+// value. The slot offset is one mask away from the store address.
 
 // Insert chunk maximum cm with entry ce into the descending list (mv, me) of
 // KC chunks under the streaming tie rule, branch-free; a chunk that does not
@@ -106,6 +105,7 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
   constexpr int KPLANE = RK * DP * 2;   // bytes of one K plane of a tile
   constexpr int TILE_BYTES = PL * KPLANE;
   constexpr int CH = tc_chunk(KC, F32);
+  static_assert(CH == 8, "list entries pack the chunk id as (first key) << 5");
   constexpr int G = CH / 4;    // float4 groups per chunk
   constexpr int RG = KC * G;   // float4 groups per row's slots
   extern __shared__ __align__(16) unsigned char tc_smem[];
@@ -182,9 +182,9 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
 #pragma unroll
   for (int m = 0; m < KC; ++m) {
     mv[m] = i < N ? -INFINITY : INFINITY;
-    me[m] = (-1 * 8) | m;  // empty, slot m
+    me[m] = (int)(0xffffff00u | (uint32_t)(m * CH * 4));  // empty, slot m
   }
-  float4* my_slots = sv + row * (RG + 1);
+  const uint32_t my_slots = tc::smem_addr(sv) + (uint32_t)(row * (RG + 1)) * 16u;
 
   const uint32_t qa = tc::smem_addr(sQ), ka = tc::smem_addr(sK);
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
@@ -276,16 +276,19 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
         // update runs for every chunk without a vote or a branch; only the
         // saved-score stores are conditional.
         const bool enter = beats<TIE_HIGH>(cm, mv[KC - 1]);
-        const int slot = entry_slot(me[KC - 1]);
+        const uint32_t soff = (uint32_t)me[KC - 1] & 0xffu;
         if (enter) {
-          float4* dst = my_slots + slot * G;
+          const uint32_t dst = my_slots + soff;
 #pragma unroll
           for (int g = 0; g < G; ++g)
-            dst[g] = make_float4(v[u * CH + 4 * g], v[u * CH + 4 * g + 1],
-                                 v[u * CH + 4 * g + 2], v[u * CH + 4 * g + 3]);
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(dst + 16u * g),
+                         "f"(v[u * CH + 4 * g]), "f"(v[u * CH + 4 * g + 1]),
+                         "f"(v[u * CH + 4 * g + 2]), "f"(v[u * CH + 4 * g + 3])
+                         : "memory");
         }
+        // chunk id (j0 + u CH) / CH in bits 8.., the slot offset below
         chunk_insert<KC, TIE_HIGH>(mv, me, cm,
-                                   (((j0 + u * CH) / CH) << 3) | slot);
+                                   (int)(((uint32_t)(j0 + u * CH) << 5) | soff));
       }
     }
     if constexpr (F32) {
@@ -321,11 +324,15 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
 #pragma unroll
   for (int m = 0; m < KC; ++m) {
     if (me[m] < 0) break;
-    const int jb = entry_id(me[m]) * CH;
-    const float4* src = my_slots + entry_slot(me[m]) * G;
+    const int jb = (me[m] >> 8) * CH;
+    const uint32_t src = my_slots + ((uint32_t)me[m] & 0xffu);
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      const float4 f = src[g];
+      float4 f;
+      asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                   : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w)
+                   : "r"(src + 16u * g)
+                   : "memory");
       buf_insert<KC, TIE_HIGH>(bs, bi, f.x, jb + 4 * g);
       buf_insert<KC, TIE_HIGH>(bs, bi, f.y, jb + 4 * g + 1);
       buf_insert<KC, TIE_HIGH>(bs, bi, f.z, jb + 4 * g + 2);

@@ -165,9 +165,6 @@ __device__ __forceinline__ void copy_tile_bf16(uint32_t base,
   }
 }
 
-__device__ __forceinline__ int entry_id(int e) { return e >> 3; }
-__device__ __forceinline__ int entry_slot(int e) { return e & 7; }
-
 // descending chunk-list insert, branch-free (the list of topk_tc.cu)
 template <int KC, bool TIE_HIGH>
 __device__ __forceinline__ void chunk_insert(float (&mv)[KC], int (&me)[KC],
@@ -238,6 +235,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
   constexpr int QPLANE = Plan::QPLANE, KPLANE = Plan::KPLANE;
   constexpr int QTILE = Plan::QTILE, KTILE = Plan::KTILE;
   constexpr int CH = 8, G = CH / 4, RG = KC * G;
+  static_assert(CH == 8, "list entries pack the chunk id as (first key) << 5");
   extern __shared__ __align__(128) unsigned char ws_smem[];
   __shared__ WsShared sh;
   unsigned char* sQ = ws_smem;
@@ -497,7 +495,11 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
     // ---------------- consumers ----------------
     const int g = warp >> 2, wq = warp & 3;
     const int row = wq * 32 + lane;  // TMEM lane
-    float4* my_slots = sv + (g * 128 + row) * (RG + 1);
+    // this row's KC saved-chunk slots (CH scores each) in shared memory;
+    // a list entry packs (chunk id << 8) | (slot * CH * 4), the slot's byte
+    // offset, so one mask gives the store address
+    const uint32_t my_slots =
+        tc::smem_addr(sv) + (uint32_t)((g * 128 + row) * (RG + 1)) * 16u;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
     const float qnan = __int_as_float(0x7fc00000);
     const float sc = p.qscale * p.post_scale;
@@ -514,7 +516,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
 #pragma unroll
       for (int m = 0; m < KC; ++m) {
         mv[m] = i < N ? -INFINITY : INFINITY;
-        me[m] = (-1 * 8) | m;  // empty, slot m
+        me[m] = (int)(0xffffff00u | (uint32_t)(m * CH * 4));  // empty, slot m
       }
       for (int j = 0; j < nkt; ++j) {
         if (!ws::wait(&sh.tfull[g], cu & 1, abort_flag)) {
@@ -550,16 +552,20 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
             cm = fmaxf(cm, v[u * CH + CH - 1]);
             // a chunk entering the list takes the slot of the entry it evicts
             const bool enter = beats<TIE_HIGH>(cm, mv[KC - 1]);
-            const int slot = ws::entry_slot(me[KC - 1]);
+            const uint32_t soff = (uint32_t)me[KC - 1] & 0xffu;
             if (enter) {
-              float4* dst = my_slots + slot * G;
+              const uint32_t dst = my_slots + soff;
 #pragma unroll
               for (int gg = 0; gg < G; ++gg)
-                dst[gg] = make_float4(v[u * CH + 4 * gg], v[u * CH + 4 * gg + 1],
-                                      v[u * CH + 4 * gg + 2], v[u * CH + 4 * gg + 3]);
+                asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(
+                                 dst + 16u * gg),
+                             "f"(v[u * CH + 4 * gg]), "f"(v[u * CH + 4 * gg + 1]),
+                             "f"(v[u * CH + 4 * gg + 2]), "f"(v[u * CH + 4 * gg + 3])
+                             : "memory");
             }
-            ws::chunk_insert<KC, TIE_HIGH>(mv, me, cm,
-                                           (((j0 + u * CH) / CH) << 3) | slot);
+            // chunk id (j0 + u CH) / CH in bits 8.., the slot offset below
+            ws::chunk_insert<KC, TIE_HIGH>(
+                mv, me, cm, (int)(((uint32_t)(j0 + u * CH) << 5) | soff));
           }
         }
       }
@@ -584,11 +590,15 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
 #pragma unroll
       for (int m = 0; m < KC; ++m) {
         if (me[m] < 0) break;
-        const int jb = ws::entry_id(me[m]) * CH;
-        const float4* src = my_slots + ws::entry_slot(me[m]) * G;
+        const int jb = (me[m] >> 8) * CH;
+        const uint32_t src = my_slots + ((uint32_t)me[m] & 0xffu);
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
-          const float4 f = src[gg];
+          float4 f;
+          asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                       : "=f"(f.x), "=f"(f.y), "=f"(f.z), "=f"(f.w)
+                       : "r"(src + 16u * gg)
+                       : "memory");
           buf_insert<KC, TIE_HIGH>(bs, bi, f.x, jb + 4 * gg);
           buf_insert<KC, TIE_HIGH>(bs, bi, f.y, jb + 4 * gg + 1);
           buf_insert<KC, TIE_HIGH>(bs, bi, f.z, jb + 4 * gg + 2);
