@@ -315,18 +315,19 @@ __device__ __forceinline__ float ex2_approx(float x) {
 // (EPV = elements per 16 bytes: 8 bf16 or 4 fp32) and each moves 16 bytes of
 // every gathered V row and of the output row, so one warp instruction touches
 // 32/(DP/EPV) whole rows rather than 32 scattered pieces. The owners first
-// prefetch their V rows into L2; the loads then go out in batches of up to 16
-// per lane before any is used. Requires d % EPV == 0 and 16-byte aligned V
-// and O rows. Every lane of the warp must call it (the row data moves by
-// shuffles).
-template <typename T, int DP, int KC>
+// prefetch their V rows into L2; the loads then go out in batches of up to
+// MAXB (16 by default) per lane before any is used — a smaller batch keeps a
+// register-limited caller from spilling. Requires d % EPV == 0 and 16-byte
+// aligned V and O rows. Every lane of the warp must call it (the row data
+// moves by shuffles).
+template <typename T, int DP, int KC, int MAXB = 16>
 __device__ __forceinline__ void coop_gather_store(
     const T* V, int64_t vn, T* O, int64_t on, int row0, int N, int d, int kk,
     const int (&idx)[KC], const float (&w)[KC], bool nan_row) {
   constexpr int EPV = 16 / (int)sizeof(T);  // elements per 16-byte piece
   constexpr int LPR = DP / EPV;             // lanes per row
   constexpr int RPI = 32 / LPR;
-  constexpr int GI = KC >= 16 ? 1 : (16 / KC < LPR ? 16 / KC : LPR);
+  constexpr int GI = KC >= MAXB ? 1 : (MAXB / KC < LPR ? MAXB / KC : LPR);
   constexpr int LINE = 128 / (int)sizeof(T);  // elements per 128-byte line
   static_assert(LPR >= 1 && LPR <= 32, "row width");
   const int lane = threadIdx.x & 31;

@@ -686,8 +686,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
 #pragma unroll
         for (int m = 0; m < KC; ++m) w[m] = (m < kk) ? e[m] / den : 0.f;
         const T* V = static_cast<const T*>(p.v) + (int64_t)b * p.st.vb;
-        tc::coop_gather_store<T, DP, KC>(V, p.st.vn, Ob, p.st.on, q0 + wq * 32, N, d,
-                                         kk, bi, w, empty);
+        // at most 8 loads in flight per lane: this kernel has 96 registers
+        tc::coop_gather_store<T, DP, KC, 8>(V, p.st.vn, Ob, p.st.on, q0 + wq * 32, N,
+                                            d, kk, bi, w, empty);
       }
     }
     if (!ok) *abort_flag = 1;
