@@ -459,6 +459,13 @@ def _comm_c1(ops, dev, stream) -> dict:
     res["fused_graph_us"], note = _graph_us(fused, dev, stream, calls=20, replays=20)
     if note:
         res["graph_note"] = note
+    # the same module shape at larger batches (persistent form above four
+    # blocks per SM), device time from CUDA graph replays
+    for Bx in (1024, 4096):
+        xb = torch.randn(Bx, N, D, generator=g).to(dev)
+        res[f"fused_graph_us_B{Bx}"], _ = _graph_us(
+            lambda s: ops.comm_forward(xb, w_qkv, b_qkv, w_p, b_p, k), dev, stream,
+            calls=20, replays=20)
     return res
 
 

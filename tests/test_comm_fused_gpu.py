@@ -57,6 +57,30 @@ def test_comm_forward_matches_module_oracle(B, N, D, m, topk):
                                atol=1e-5)
 
 
+@pytest.mark.parametrize("B,N,D,m,topk", [
+    (4096, 6, 64, 16, 2), (4096, 6, 64, 16, 0), (1000, 32, 36, 8, 3),
+    (3001, 17, 64, 32, 1)])
+def test_comm_forward_large_batches(B, N, D, m, topk):
+    """Batches above four blocks per SM take the persistent form (weights
+    staged once per block, x tiles double-buffered): every episode matches
+    the oracle, and a slice of the batch run on its own (one block per
+    episode) gives the same bits."""
+    from tarmac_b200 import ops
+    x = torch.randn(B, N, D, generator=torch.Generator().manual_seed(B + N))
+    w = [t.cuda() for t in _weights(D, m, seed=m + topk + 1)]
+    xc = x.cuda()
+    out = ops.comm_forward(xc, *w, topk)
+    sel = np.sort(np.random.default_rng(B).choice(B, size=64, replace=False))
+    ref, q, k = oracle.comm_forward(x.numpy()[sel], *(t.cpu().numpy() for t in w),
+                                    topk)
+    ok = ~_near_tie_rows(q, k, topk)
+    assert ok.mean() > 0.99
+    np.testing.assert_allclose(out.cpu().numpy()[sel][ok], ref[ok], rtol=1e-5,
+                               atol=1e-5)
+    head = ops.comm_forward(xc[:16].contiguous(), *w, topk)
+    assert torch.equal(head, out[:16])
+
+
 @pytest.mark.parametrize("mode,k", [("topk", 2), ("topk_gather", 3),
                                     ("dense", 0), ("dense_sdpa", 0)])
 def test_module_inference_uses_one_kernel_with_same_result(mode, k):

@@ -83,87 +83,67 @@ __host__ __device__ __forceinline__ int comm_row_stride(int D, bool vec) {
 // thread (agent, r) forms output column r. Larger episodes give each thread
 // whole query agents. Both forms evaluate every output with the same
 // operations in the same order.
-template <int MP, int KM, bool VEC>
-__global__ void __launch_bounds__(COMM_THREADS, 1) comm_forward_kernel(CommParams p) {
-  extern __shared__ __align__(16) float comm_sm[];
-  const int N = p.N, D = p.in_dim, m = p.m;
-  const int DS = comm_row_stride(D, VEC);
-  const int M3 = 3 * m;
-  float* sq = comm_sm;
-  float* sk = sq + (size_t)N * MP;
-  float* sv = sk + (size_t)N * MP;
-  float* sx = sv + (size_t)N * MP;
-  float* sg = sx + (size_t)COMM_XTILE * DS;
-  float* sw = sg + COMM_THREADS;
-  float* spw = sw + (p.w_smem ? (size_t)M3 * DS : 0);
-  float* spb = spw + m * m;
-  float* sbq = spb + m;
-  const int b = blockIdx.x;
-  const float* X = p.x + (int64_t)b * N * D;
-
-  // weights and biases: every copy issued before the first wait
-  if (p.w_smem) comm_stage<VEC>(sw, DS, p.wqkv, M3, D);
-  for (int e = threadIdx.x; e < m * m; e += blockDim.x) cp_async4(spw + e, p.wproj + e);
-  for (int e = threadIdx.x; e < m; e += blockDim.x) cp_async4(spb + e, p.bproj + e);
-  for (int e = threadIdx.x; e < M3; e += blockDim.x) cp_async4(sbq + e, p.bqkv + e);
-  if (m < MP)
-    for (int e = threadIdx.x; e < 3 * N * MP; e += blockDim.x) sq[e] = 0.f;
-
-  // ---- phase 1: q, k, v rows of every agent --------------------------------
-  // Threads take (row, output) pairs of the staged tile, consecutive threads
-  // consecutive outputs of one row: the x row is a broadcast read, the
-  // weight rows distinct banks. The dot product runs over the columns in
-  // order, then adds the bias.
-  for (int r0 = 0; r0 < N; r0 += COMM_XTILE) {
-    const int nr = min(COMM_XTILE, N - r0);
-    __syncthreads();  // the previous tile is consumed
-    comm_stage<VEC>(sx, DS, X + (int64_t)r0 * D, nr, D);
-    cp_async_wait_all();
-    __syncthreads();
-    for (int pr = threadIdx.x; pr < nr * M3; pr += blockDim.x) {
-      const int rr = pr / M3, o = pr - rr * M3;
-      const float* xr = sx + rr * DS;
-      float acc = 0.f;
-      if constexpr (VEC) {
-        if (p.w_smem) {
-          const float* wr = sw + o * DS;
-          for (int c = 0; c < D; c += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(xr + c);
-            const float4 w = *reinterpret_cast<const float4*>(wr + c);
-            acc = fmaf(a.x, w.x, acc);
-            acc = fmaf(a.y, w.y, acc);
-            acc = fmaf(a.z, w.z, acc);
-            acc = fmaf(a.w, w.w, acc);
-          }
-        } else {
-          const float4* wr = reinterpret_cast<const float4*>(p.wqkv + (int64_t)o * D);
-          for (int c = 0; c < D; c += 4) {
-            const float4 a = *reinterpret_cast<const float4*>(xr + c);
-            const float4 w = __ldg(wr + (c >> 2));
-            acc = fmaf(a.x, w.x, acc);
-            acc = fmaf(a.y, w.y, acc);
-            acc = fmaf(a.z, w.z, acc);
-            acc = fmaf(a.w, w.w, acc);
-          }
+// Phase 1 for the staged x rows [r0, r0 + nr) (x tile sx, row stride DS):
+// threads take (row, output) pairs, consecutive threads consecutive outputs
+// of one row, so the x row is a broadcast read and the weight rows hit
+// distinct banks. Each dot product runs over the columns in order, then
+// adds the bias.
+template <int MP, bool VEC>
+__device__ __forceinline__ void comm_project(const CommParams& p, const float* sx,
+                                             int DS, const float* sw,
+                                             const float* sbq, int r0, int nr,
+                                             float* sq, float* sk, float* sv) {
+  const int D = p.in_dim, m = p.m, M3 = 3 * m;
+  for (int pr = threadIdx.x; pr < nr * M3; pr += blockDim.x) {
+    const int rr = pr / M3, o = pr - rr * M3;
+    const float* xr = sx + rr * DS;
+    float acc = 0.f;
+    if constexpr (VEC) {
+      if (p.w_smem) {
+        const float* wr = sw + o * DS;
+        for (int c = 0; c < D; c += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(xr + c);
+          const float4 w = *reinterpret_cast<const float4*>(wr + c);
+          acc = fmaf(a.x, w.x, acc);
+          acc = fmaf(a.y, w.y, acc);
+          acc = fmaf(a.z, w.z, acc);
+          acc = fmaf(a.w, w.w, acc);
         }
       } else {
-        if (p.w_smem) {
-          const float* wr = sw + o * DS;
-          for (int c = 0; c < D; ++c) acc = fmaf(xr[c], wr[c], acc);
-        } else {
-          const float* wr = p.wqkv + (int64_t)o * D;
-          for (int c = 0; c < D; ++c) acc = fmaf(xr[c], __ldg(wr + c), acc);
+        const float4* wr = reinterpret_cast<const float4*>(p.wqkv + (int64_t)o * D);
+        for (int c = 0; c < D; c += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(xr + c);
+          const float4 w = __ldg(wr + (c >> 2));
+          acc = fmaf(a.x, w.x, acc);
+          acc = fmaf(a.y, w.y, acc);
+          acc = fmaf(a.z, w.z, acc);
+          acc = fmaf(a.w, w.w, acc);
         }
       }
-      acc += sbq[o];
-      const int part = o / m, col = o - part * m;
-      float* dst = part == 0 ? sq : (part == 1 ? sk : sv);
-      dst[(r0 + rr) * MP + col] = acc;
+    } else {
+      if (p.w_smem) {
+        const float* wr = sw + o * DS;
+        for (int c = 0; c < D; ++c) acc = fmaf(xr[c], wr[c], acc);
+      } else {
+        const float* wr = p.wqkv + (int64_t)o * D;
+        for (int c = 0; c < D; ++c) acc = fmaf(xr[c], __ldg(wr + c), acc);
+      }
     }
+    acc += sbq[o];
+    const int part = o / m, col = o - part * m;
+    float* dst = part == 0 ? sq : (part == 1 ? sk : sv);
+    dst[(r0 + rr) * MP + col] = acc;
   }
-  __syncthreads();
+}
 
-  // ---- phase 2: attention, GELU, projection --------------------------------
+// Phase 2 for episode b: attention over the episode's q, k, v rows, GELU and
+// the output projection (both forms described above).
+template <int MP, int KM>
+__device__ __forceinline__ void comm_attend(const CommParams& p, int b,
+                                            const float* sq, const float* sk,
+                                            const float* sv, float* sg,
+                                            const float* spw, const float* spb) {
+  const int N = p.N, m = p.m;
   if (N * MP <= COMM_THREADS) {
     // one thread per (agent i, message column c)
     const int i = threadIdx.x / MP, c = threadIdx.x % MP;
@@ -324,6 +304,95 @@ __global__ void __launch_bounds__(COMM_THREADS, 1) comm_forward_kernel(CommParam
   }
 }
 
+template <int MP, int KM, bool VEC>
+__global__ void __launch_bounds__(COMM_THREADS, 1) comm_forward_kernel(CommParams p) {
+  extern __shared__ __align__(16) float comm_sm[];
+  const int N = p.N, D = p.in_dim, m = p.m;
+  const int DS = comm_row_stride(D, VEC);
+  const int M3 = 3 * m;
+  float* sq = comm_sm;
+  float* sk = sq + (size_t)N * MP;
+  float* sv = sk + (size_t)N * MP;
+  float* sx = sv + (size_t)N * MP;
+  float* sg = sx + (size_t)COMM_XTILE * DS;
+  float* sw = sg + COMM_THREADS;
+  float* spw = sw + (p.w_smem ? (size_t)M3 * DS : 0);
+  float* spb = spw + m * m;
+  float* sbq = spb + m;
+  const int b = blockIdx.x;
+  const float* X = p.x + (int64_t)b * N * D;
+
+  // weights and biases: every copy issued before the first wait
+  if (p.w_smem) comm_stage<VEC>(sw, DS, p.wqkv, M3, D);
+  for (int e = threadIdx.x; e < m * m; e += blockDim.x) cp_async4(spw + e, p.wproj + e);
+  for (int e = threadIdx.x; e < m; e += blockDim.x) cp_async4(spb + e, p.bproj + e);
+  for (int e = threadIdx.x; e < M3; e += blockDim.x) cp_async4(sbq + e, p.bqkv + e);
+  if (m < MP)
+    for (int e = threadIdx.x; e < 3 * N * MP; e += blockDim.x) sq[e] = 0.f;
+
+  // ---- phase 1: q, k, v rows of every agent, 32 staged x rows at a time ----
+  for (int r0 = 0; r0 < N; r0 += COMM_XTILE) {
+    const int nr = min(COMM_XTILE, N - r0);
+    __syncthreads();  // the previous tile is consumed
+    comm_stage<VEC>(sx, DS, X + (int64_t)r0 * D, nr, D);
+    cp_async_wait_all();
+    __syncthreads();
+    comm_project<MP, VEC>(p, sx, DS, sw, sbq, r0, nr, sq, sk, sv);
+  }
+  __syncthreads();
+
+  // ---- phase 2: attention, GELU, projection --------------------------------
+  comm_attend<MP, KM>(p, b, sq, sk, sv, sg, spw, spb);
+}
+
+// Persistent form for large batches of short episodes (N <= 32, W_qkv in
+// shared memory): a block stages the weights once and loops over episodes
+// b = blockIdx.x, blockIdx.x + gridDim.x, ...; the next episode's x rows are
+// copied into the second of two x tiles while the current episode is
+// projected and attended. Each episode's outputs are those of
+// comm_forward_kernel (same functions, same order of operations).
+template <int MP, int KM, bool VEC>
+__global__ void __launch_bounds__(COMM_THREADS, 4) comm_persist_kernel(CommParams p) {
+  extern __shared__ __align__(16) float comm_sm[];
+  const int N = p.N, D = p.in_dim, m = p.m;
+  const int DS = comm_row_stride(D, VEC);
+  const int M3 = 3 * m;
+  float* sq = comm_sm;
+  float* sk = sq + (size_t)N * MP;
+  float* sv = sk + (size_t)N * MP;
+  float* sx = sv + (size_t)N * MP;  // two tiles of COMM_XTILE rows
+  float* sg = sx + (size_t)2 * COMM_XTILE * DS;
+  float* sw = sg + COMM_THREADS;
+  float* spw = sw + (size_t)M3 * DS;
+  float* spb = spw + m * m;
+  float* sbq = spb + m;
+
+  comm_stage<VEC>(sw, DS, p.wqkv, M3, D);
+  for (int e = threadIdx.x; e < m * m; e += blockDim.x) cp_async4(spw + e, p.wproj + e);
+  for (int e = threadIdx.x; e < m; e += blockDim.x) cp_async4(spb + e, p.bproj + e);
+  for (int e = threadIdx.x; e < M3; e += blockDim.x) cp_async4(sbq + e, p.bqkv + e);
+  if (m < MP)
+    for (int e = threadIdx.x; e < 3 * N * MP; e += blockDim.x) sq[e] = 0.f;
+  int cur = 0;
+  if ((int)blockIdx.x < p.B)
+    comm_stage<VEC>(sx, DS, p.x + (int64_t)blockIdx.x * N * D, N, D);
+  for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
+    cp_async_wait_all();  // this episode's x rows (and, first, the weights)
+    __syncthreads();
+    const int nb = b + gridDim.x;
+    if (nb < p.B)
+      comm_stage<VEC>(sx + (size_t)(cur ^ 1) * COMM_XTILE * DS, DS,
+                      p.x + (int64_t)nb * N * D, N, D);
+    comm_project<MP, VEC>(p, sx + (size_t)cur * COMM_XTILE * DS, DS, sw, sbq, 0, N,
+                          sq, sk, sv);
+    __syncthreads();
+    comm_attend<MP, KM>(p, b, sq, sk, sv, sg, spw, spb);
+    __syncthreads();  // q, k, v, the GELU buffer and this x tile are free
+    cur ^= 1;
+  }
+  cp_async_wait_all();
+}
+
 size_t comm_smem_bytes(int N, int in_dim, int m, int MP, bool vec) {
   return sizeof(float) * ((size_t)m * m + 4 * (size_t)m + (size_t)3 * N * MP +
                           (size_t)COMM_XTILE * comm_row_stride(in_dim, vec) +
@@ -345,7 +414,23 @@ static cudaError_t launch_comm_t(CommParams p, cudaStream_t s) {
       sizeof(float) * (size_t)3 * p.m * comm_row_stride(p.in_dim, VEC);
   p.w_smem = sm + wb <= COMM_SMEM_WITH_W;
   if (p.w_smem) sm += wb;
-  cudaError_t e = raise_smem_limit(
+  // Large batches of short episodes: the persistent form stages the weights
+  // once per block instead of once per episode (B=4096, N=6: 41 us with one
+  // block per episode).
+  int dev = 0, nsm = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return e;
+  const int pgrid = 4 * nsm;
+  const size_t psm = sm + sizeof(float) * (size_t)COMM_XTILE * comm_row_stride(p.in_dim, VEC);
+  if (p.w_smem && p.N <= COMM_XTILE && p.B > pgrid && 4 * psm <= 220 * 1024) {
+    e = raise_smem_limit((const void*)comm_persist_kernel<MP, KM, VEC>, psm);
+    if (e != cudaSuccess) return e;
+    comm_persist_kernel<MP, KM, VEC><<<pgrid, COMM_THREADS, psm, s>>>(p);
+    return cudaGetLastError();
+  }
+  e = raise_smem_limit(
       (const void*)comm_forward_kernel<MP, KM, VEC>, (size_t)(sm));
   if (e != cudaSuccess) return e;
   comm_forward_kernel<MP, KM, VEC><<<p.B, COMM_THREADS, sm, s>>>(p);

@@ -169,6 +169,23 @@ __device__ __forceinline__ float max3f(float a, float b, float c) {
   return d;
 }
 
+// Maximum of CH (8 or 16) consecutive values as a shallow tree of
+// three-input maxima (dependency depth 2 or 3 instead of a chain); max is
+// exact, so the result equals the chain's (NaN inputs are skipped alike).
+template <int CH>
+__device__ __forceinline__ float chunk_max(const float* v) {
+  static_assert(CH == 8 || CH == 16, "8- or 16-value chunks");
+  if constexpr (CH == 8) {
+    return max3f(max3f(v[0], v[1], v[2]), max3f(v[3], v[4], v[5]),
+                 fmaxf(v[6], v[7]));
+  } else {
+    const float a = max3f(v[0], v[1], v[2]), b = max3f(v[3], v[4], v[5]);
+    const float c = max3f(v[6], v[7], v[8]), e = max3f(v[9], v[10], v[11]);
+    const float f = max3f(v[12], v[13], v[14]);
+    return fmaxf(max3f(a, b, c), max3f(e, f, v[15]));
+  }
+}
+
 // q (as DP/2 column pairs) . one fp32 row in shared memory (16-byte aligned):
 // even and odd columns accumulate in the two halves, added at the end. Every
 // caller forms a given score through this one function, so a score is

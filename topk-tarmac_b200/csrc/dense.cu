@@ -245,11 +245,17 @@ bool dense_tc_supported(const AttnParams& p);
 cudaError_t launch_dense_tc(const AttnParams& p, cudaStream_t s);
 bool dense_tc_f32_supported(const AttnParams& p);
 cudaError_t launch_dense_tc_f32(const AttnParams& p, cudaStream_t s);
+bool dense_ws_supported(const AttnParams& p);
+cudaError_t launch_dense_ws(const AttnParams& p, cudaStream_t s);
 
-// Episodes of 128 or more agents run on the tensor cores (dense_tc.cu): bf16
-// directly, fp32 with d in {8, 16} and 16-byte rows as three exact bf16
-// planes; other shapes on the packed-FMA kernel above.
+// Episodes of 128 or more agents run on the tensor cores: bf16 directly —
+// large batches of 385-512-agent episodes with d from 24 to 64 in the
+// persistent warp-specialized kernel (dense_ws.cu), others one 128-query
+// block at a time (dense_tc.cu), the same bits either way — and fp32 with d
+// in {8, 16} and 16-byte rows as three exact bf16 planes; other shapes on
+// the packed-FMA kernel above.
 cudaError_t launch_dense(const AttnParams& p, int dtype, cudaStream_t s) {
+  if (dtype == TARMAC_BF16 && dense_ws_supported(p)) return launch_dense_ws(p, s);
   if (dtype == TARMAC_BF16 && dense_tc_supported(p))
     return launch_dense_tc(p, s);
   if (dtype == TARMAC_F32 && dense_tc_f32_supported(p))

@@ -266,11 +266,7 @@ __global__ void __launch_bounds__(TC_THREADS, DP >= 128 ? 2 : 4)
       }
 #pragma unroll
       for (int u = 0; u < 32 / CH; ++u) {
-        float cm = v[u * CH];
-#pragma unroll
-        for (int t = 1; t + 1 < CH; t += 2)
-          cm = max3f(cm, v[u * CH + t], v[u * CH + t + 1]);
-        cm = fmaxf(cm, v[u * CH + CH - 1]);
+        const float cm = chunk_max<CH>(v + u * CH);
         // A chunk entering the list takes the slot of the entry it evicts.
         // Almost every chunk admits some lane of the warp, so the list
         // update runs for every chunk without a vote or a branch; only the

@@ -28,8 +28,8 @@
 // shared abort flag that the other roles poll, so every role ends, frees
 // nothing it does not own, and the block frees its TMEM; rows of an aborted
 // episode are not written.
-#include "tc_common.cuh"
 #include "topk_chunk.cuh"
+#include "ws_common.cuh"
 
 namespace tarmac {
 
@@ -46,50 +46,9 @@ constexpr int WS_NQ = 4;                 // query tiles per episode (max)
 constexpr int WS_MAX_N = WS_NQ * 128;
 constexpr int WS_NR = 4;                 // fp32 raw slots per producer ring
 constexpr int WS_RAWB = 64 * 16 * 4;     // one raw slot: 64 fp32 rows of 16
-constexpr uint32_t WS_WAIT_LIMIT = 1u << 22;
 constexpr size_t WS_SMEM_LIMIT = 230 * 1024;
 
 namespace ws {
-
-// Bounded mbarrier wait that also gives up once another role aborted.
-__device__ __forceinline__ bool wait(uint64_t* mbar, uint32_t parity,
-                                     volatile int* abort_flag) {
-  const uint32_t a = tc::smem_addr(mbar);
-  for (uint32_t it = 0; it < WS_WAIT_LIMIT; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n.reg .pred p;\nmbarrier.try_wait.parity.shared::cta.b64 p, [%1], "
-        "%2;\nselp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(a), "r"(parity)
-        : "memory");
-    if (done) return true;
-    if ((it & 63) == 63 && *abort_flag) return false;
-  }
-  *abort_flag = 1;
-  return false;
-}
-
-__device__ __forceinline__ void arrive(uint64_t* mbar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(
-                   tc::smem_addr(mbar))
-               : "memory");
-}
-
-// 16-byte piece e of an R-row tile with KCH chunks per row, in the K-major
-// core-matrix order: it sits at byte 16 e and holds row
-// ((e / 8) / KCH) * 8 + e % 8, columns 8 c .. 8 c + 7 with c = (e / 8) % KCH.
-template <int KCH>
-__device__ __forceinline__ void piece_rc(int e, int& r, int& c) {
-  r = ((e >> 3) / KCH) * 8 + (e & 7);
-  c = (e >> 3) % KCH;
-}
-
-__device__ __forceinline__ void cp16(uint32_t dst, const void* src, bool ok) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst),
-               "l"(src), "r"(ok ? 16u : 0u)
-               : "memory");
-}
 
 // fp32 (16 columns): the pieces e = tid + NT u of a 64-row item (128 pieces
 // of 8 values) into a raw slot (piece e at byte 32 e); rows >= nvalid and
@@ -147,24 +106,6 @@ __device__ __forceinline__ void split_raw(uint32_t base, uint32_t plane,
   }
 }
 
-// bf16: rows [0, R) of src (row stride rs, d % 8 == 0) straight into a
-// K-major tile of DP columns by NT threads; rows >= nvalid and columns >= d
-// zero-filled.
-template <int DP, int R, int NT>
-__device__ __forceinline__ void copy_tile_bf16(uint32_t base,
-                                               const __nv_bfloat16* src,
-                                               int64_t rs, int nvalid, int d,
-                                               int tid) {
-  constexpr int KCH = DP / 8;
-#pragma unroll 4
-  for (int e = tid; e < R * KCH; e += NT) {
-    int r, c;
-    piece_rc<KCH>(e, r, c);
-    const bool ok = r < nvalid && c * 8 < d;
-    cp16(base + (uint32_t)e * 16u, ok ? src + (int64_t)r * rs + c * 8 : src, ok);
-  }
-}
-
 // descending chunk-list insert, branch-free (the list of topk_tc.cu)
 template <int KC, bool TIE_HIGH>
 __device__ __forceinline__ void chunk_insert(float (&mv)[KC], int (&me)[KC],
@@ -196,7 +137,7 @@ struct WsShared {
 // current one runs), a two-slot ring of 128-key K tiles, fp32 raw rings (K
 // producers, Q producer), the consumers' saved chunks, and the episode's V
 // rows when they fit (VST).
-template <typename T, int DP, int KC>
+template <typename T, int DP, int KC, int CH>
 struct WsPlan {
   static constexpr bool F32 = sizeof(T) == 4;
   static constexpr int PL = F32 ? 3 : 1;       // bf16 planes per operand
@@ -207,7 +148,7 @@ struct WsPlan {
   static constexpr int KTILE = PL * KPLANE;
   static constexpr int KBYTES = WS_NS * KTILE;
   static constexpr int RAWBYTES = F32 ? 2 * WS_NR * WS_RAWB : 0;
-  static constexpr int SVBYTES = WS_MAX_N * (KC * 8 + 4) * 4;
+  static constexpr int SVBYTES = WS_MAX_N * (KC * CH + 4) * 4;
   static constexpr int VROW = DP * (int)sizeof(T);
   static constexpr int VALL = WS_MAX_N * VROW;
   static constexpr int REST = KBYTES + RAWBYTES + SVBYTES;
@@ -226,16 +167,19 @@ struct WsPlan {
   static constexpr uint32_t QFULL = F32 ? 2 : 1;   // per Q tile
 };
 
-template <typename T, int DP, int KC, bool TIE_HIGH>
+template <typename T, int DP, int KC, int CH, bool TIE_HIGH>
 __global__ void __launch_bounds__(WS_THREADS, 1)
     topk_ws_kernel(AttnParams p) {
-  using Plan = WsPlan<T, DP, KC>;
+  using Plan = WsPlan<T, DP, KC, CH>;
   constexpr bool F32 = Plan::F32;
   constexpr int KCH = Plan::KCH;
   constexpr int QPLANE = Plan::QPLANE, KPLANE = Plan::KPLANE;
   constexpr int QTILE = Plan::QTILE, KTILE = Plan::KTILE;
-  constexpr int CH = 8, G = CH / 4, RG = KC * G;
-  static_assert(CH == 8, "list entries pack the chunk id as (first key) << 5");
+  constexpr int G = CH / 4, RG = KC * G;
+  static_assert(CH == 8 || CH == 16, "8- or 16-key chunks");
+  // a list entry packs (first key of the chunk) << 5 | slot byte offset;
+  // the offset stays below CH * 32
+  constexpr uint32_t SMASK = (uint32_t)CH * 32u - 1u;
   extern __shared__ __align__(128) unsigned char ws_smem[];
   __shared__ WsShared sh;
   unsigned char* sQ = ws_smem;
@@ -435,11 +379,14 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
     asm volatile("cp.async.wait_all;" ::: "memory");
   } else if (warp == WS_MMA_WARP) {
     // ---------------- MMA issuer ----------------
+    // Event-driven: each group's product for tile j is issued as soon as the
+    // group has read tile j - 1 and K_j has landed, so a slow group holds up
+    // no other; a K slot is released once every group's product of its tile
+    // has been issued. The per-group state is unrolled into registers.
     // Descriptors are formed once; plane, K-step and tile offsets are added
     // to the 14-bit address field (addresses stay below 256 KB: no carry).
     if (lane == 0) {
       uint32_t kcount = 0;
-      uint32_t tu[WS_NQ] = {0, 0, 0, 0};
       const uint32_t idesc = tc::idesc_bf16(128, WS_RK, false, false);
       const uint64_t dq0 = tc::smem_desc(qa, 128, KCH * 128);
       const uint64_t dk0 = tc::smem_desc(ka, 128, KCH * 128);
@@ -449,13 +396,24 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
         const uint32_t use = (uint32_t)(it / Plan::NQB);
         for (int g = 0; g < nqt; ++g)
           if (!ws::wait(&sh.qfull[qb][g], use & 1, abort_flag)) goto mma_done;
-        for (int j = 0; j < nkt; ++j, ++kcount) {
-          const int s = kcount % WS_NS;
-          if (!ws::wait(&sh.kfull[s], (kcount / WS_NS) & 1, abort_flag)) goto mma_done;
-          const uint64_t dk = dk0 + (uint64_t)((s * KTILE) >> 4);
-          for (int g = 0; g < nqt; ++g) {
-            if (!ws::wait(&sh.tempty[g], (tu[g] & 1) ^ 1, abort_flag)) goto mma_done;
+        int nx[WS_NQ] = {0, 0, 0, 0};   // next tile of each group
+        uint32_t issued = 0;            // per slot (8 bits): groups issued
+        int finished = 0;
+        uint32_t idle = 0;
+        while (finished < nqt) {
+          bool progress = false;
+#pragma unroll
+          for (int g = 0; g < WS_NQ; ++g) {
+            if (g >= nqt || nx[g] == nkt) continue;
+            // the TMEM quarter's uses so far: one per tile of earlier episodes
+            const uint32_t tu = (uint32_t)(kcount + nx[g]);
+            const uint32_t kj = kcount + (uint32_t)nx[g];
+            const int s = kj % WS_NS;
+            if (!ws::test(&sh.tempty[g], (tu & 1) ^ 1) ||
+                !ws::test(&sh.kfull[s], (kj / WS_NS) & 1))
+              continue;
             tc::fence_after_sync();
+            const uint64_t dk = dk0 + (uint64_t)((s * KTILE) >> 4);
             const uint64_t dq = dq0 + (uint64_t)((qb * WS_NQ * QTILE + g * QTILE) >> 4);
             const uint32_t td = tmem + g * 128;
 #pragma unroll
@@ -474,10 +432,22 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
               }
             }
             tc::mma_commit(&sh.tfull[g]);
-            ++tu[g];
+            issued += 1u << (8 * s);
+            if (((issued >> (8 * s)) & 0xffu) == (uint32_t)nqt) {
+              issued &= ~(0xffu << (8 * s));
+              tc::mma_commit(&sh.kempty[s]);
+            }
+            if (++nx[g] == nkt) ++finished;
+            progress = true;
           }
-          tc::mma_commit(&sh.kempty[s]);
+          if (progress) {
+            idle = 0;
+          } else if (++idle > WS_WAIT_LIMIT || *abort_flag) {
+            *abort_flag = 1;
+            goto mma_done;
+          }
         }
+        kcount += (uint32_t)nkt;
         for (int g = 0; g < nqt; ++g) tc::mma_commit(&sh.qempty[qb][g]);
       }
       // drain: the last episode's products and commits have landed before
@@ -495,9 +465,9 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
     // ---------------- consumers ----------------
     const int g = warp >> 2, wq = warp & 3;
     const int row = wq * 32 + lane;  // TMEM lane
-    // this row's KC saved-chunk slots (CH scores each) in shared memory;
-    // a list entry packs (chunk id << 8) | (slot * CH * 4), the slot's byte
-    // offset, so one mask gives the store address
+    // this row's KC saved-chunk slots (CH scores each) in shared memory; a
+    // list entry carries its slot's byte offset (slot * CH * 4) in the low
+    // bits, so one mask gives the store address
     const uint32_t my_slots =
         tc::smem_addr(sv) + (uint32_t)((g * 128 + row) * (RG + 1)) * 16u;
     const uint32_t lane_off = (uint32_t)(wq * 32) << 16;
@@ -516,7 +486,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
 #pragma unroll
       for (int m = 0; m < KC; ++m) {
         mv[m] = i < N ? -INFINITY : INFINITY;
-        me[m] = (int)(0xffffff00u | (uint32_t)(m * CH * 4));  // empty, slot m
+        me[m] = (int)(~SMASK | (uint32_t)(m * CH * 4));  // empty, slot m
       }
       for (int j = 0; j < nkt; ++j) {
         if (!ws::wait(&sh.tfull[g], cu & 1, abort_flag)) {
@@ -545,14 +515,10 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
           }
 #pragma unroll
           for (int u = 0; u < 32 / CH; ++u) {
-            float cm = v[u * CH];
-#pragma unroll
-            for (int t = 1; t + 1 < CH; t += 2)
-              cm = max3f(cm, v[u * CH + t], v[u * CH + t + 1]);
-            cm = fmaxf(cm, v[u * CH + CH - 1]);
+            const float cm = chunk_max<CH>(v + u * CH);
             // a chunk entering the list takes the slot of the entry it evicts
             const bool enter = beats<TIE_HIGH>(cm, mv[KC - 1]);
-            const uint32_t soff = (uint32_t)me[KC - 1] & 0xffu;
+            const uint32_t soff = (uint32_t)me[KC - 1] & SMASK;
             if (enter) {
               const uint32_t dst = my_slots + soff;
 #pragma unroll
@@ -563,7 +529,7 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
                              "f"(v[u * CH + 4 * gg + 2]), "f"(v[u * CH + 4 * gg + 3])
                              : "memory");
             }
-            // chunk id (j0 + u CH) / CH in bits 8.., the slot offset below
+            // the chunk's first key in bits 5.., the slot offset below
             ws::chunk_insert<KC, TIE_HIGH>(
                 mv, me, cm, (int)(((uint32_t)(j0 + u * CH) << 5) | soff));
           }
@@ -590,8 +556,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
 #pragma unroll
       for (int m = 0; m < KC; ++m) {
         if (me[m] < 0) break;
-        const int jb = (me[m] >> 8) * CH;
-        const uint32_t src = my_slots + ((uint32_t)me[m] & 0xffu);
+        const int jb = (me[m] >> 5) & ~(CH - 1);
+        const uint32_t src = my_slots + ((uint32_t)me[m] & SMASK);
 #pragma unroll
         for (int gg = 0; gg < G; ++gg) {
           float4 f;
@@ -700,11 +666,16 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
 
 template <typename T, int DP, int KC, bool TIE_HIGH>
 static cudaError_t launch_ws_t(const AttnParams& p, cudaStream_t s) {
-  using Plan = WsPlan<T, DP, KC>;
+#ifdef WS_FORCE_CH
+  constexpr int CH = WS_FORCE_CH;
+#else
+  constexpr int CH = 8;
+#endif
+  using Plan = WsPlan<T, DP, KC, CH>;
   if constexpr (!Plan::FITS) {
     return cudaErrorInvalidConfiguration;
   } else {
-    const void* fn = (const void*)topk_ws_kernel<T, DP, KC, TIE_HIGH>;
+    const void* fn = (const void*)topk_ws_kernel<T, DP, KC, CH, TIE_HIGH>;
     cudaError_t e = raise_smem_limit(fn, (size_t)Plan::TOTAL);
     if (e != cudaSuccess) return e;
     int dev = 0, nsm = 0;
@@ -714,7 +685,7 @@ static cudaError_t launch_ws_t(const AttnParams& p, cudaStream_t s) {
     if (e != cudaSuccess) return e;
     const int grid = p.B < nsm ? p.B : nsm;
     if (grid <= 0) return cudaSuccess;
-    topk_ws_kernel<T, DP, KC, TIE_HIGH><<<grid, WS_THREADS, Plan::TOTAL, s>>>(p);
+    topk_ws_kernel<T, DP, KC, CH, TIE_HIGH><<<grid, WS_THREADS, Plan::TOTAL, s>>>(p);
     return cudaGetLastError();
   }
 }
