@@ -18,6 +18,8 @@
 // sorted k-best buffer (top-k) or a base-2 online softmax (dense), the V
 // aggregate, GELU and the output projection. Sized for the reference's
 // MAPPO shapes (N up to 1024, msg_dim up to 64, in_dim up to 256).
+#include <algorithm>
+
 #include "comm.cuh"
 #include "topk_chunk.cuh"
 
@@ -25,6 +27,8 @@ namespace tarmac {
 
 constexpr int COMM_THREADS = 128;
 constexpr int COMM_XTILE = 32;  // x rows staged per step
+// resident blocks per SM of the persistent form for large batches
+constexpr int COMM_PERSIST_BPS = 8;
 
 
 
@@ -352,7 +356,7 @@ __global__ void __launch_bounds__(COMM_THREADS, 1) comm_forward_kernel(CommParam
 // projected and attended. Each episode's outputs are those of
 // comm_forward_kernel (same functions, same order of operations).
 template <int MP, int KM, bool VEC>
-__global__ void __launch_bounds__(COMM_THREADS, 4) comm_persist_kernel(CommParams p) {
+__global__ void __launch_bounds__(COMM_THREADS, COMM_PERSIST_BPS) comm_persist_kernel(CommParams p) {
   extern __shared__ __align__(16) float comm_sm[];
   const int N = p.N, D = p.in_dim, m = p.m;
   const int DS = comm_row_stride(D, VEC);
@@ -360,8 +364,8 @@ __global__ void __launch_bounds__(COMM_THREADS, 4) comm_persist_kernel(CommParam
   float* sq = comm_sm;
   float* sk = sq + (size_t)N * MP;
   float* sv = sk + (size_t)N * MP;
-  float* sx = sv + (size_t)N * MP;  // two tiles of COMM_XTILE rows
-  float* sg = sx + (size_t)2 * COMM_XTILE * DS;
+  float* sx = sv + (size_t)N * MP;  // two tiles of N rows
+  float* sg = sx + (size_t)2 * N * DS;
   float* sw = sg + COMM_THREADS;
   float* spw = sw + (size_t)M3 * DS;
   float* spb = spw + m * m;
@@ -381,9 +385,9 @@ __global__ void __launch_bounds__(COMM_THREADS, 4) comm_persist_kernel(CommParam
     __syncthreads();
     const int nb = b + gridDim.x;
     if (nb < p.B)
-      comm_stage<VEC>(sx + (size_t)(cur ^ 1) * COMM_XTILE * DS, DS,
+      comm_stage<VEC>(sx + (size_t)(cur ^ 1) * N * DS, DS,
                       p.x + (int64_t)nb * N * D, N, D);
-    comm_project<MP, VEC>(p, sx + (size_t)cur * COMM_XTILE * DS, DS, sw, sbq, 0, N,
+    comm_project<MP, VEC>(p, sx + (size_t)cur * N * DS, DS, sw, sbq, 0, N,
                           sq, sk, sv);
     __syncthreads();
     comm_attend<MP, KM>(p, b, sq, sk, sv, sg, spw, spb);
@@ -422,9 +426,14 @@ static cudaError_t launch_comm_t(CommParams p, cudaStream_t s) {
   if (e != cudaSuccess) return e;
   e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  const int pgrid = 4 * nsm;
-  const size_t psm = sm + sizeof(float) * (size_t)COMM_XTILE * comm_row_stride(p.in_dim, VEC);
-  if (p.w_smem && p.N <= COMM_XTILE && p.B > pgrid && 4 * psm <= 220 * 1024) {
+  // at least two episodes per block, at most COMM_PERSIST_BPS blocks per SM
+  const int pgrid = std::min(COMM_PERSIST_BPS * nsm, p.B / 2);
+  const size_t psm = sizeof(float) * ((size_t)p.m * p.m + 4 * (size_t)p.m +
+                                      (size_t)3 * p.N * MP +
+                                      (size_t)2 * p.N * comm_row_stride(p.in_dim, VEC) +
+                                      COMM_THREADS) + wb;
+  if (p.w_smem && p.N <= COMM_XTILE && p.B >= 4 * nsm &&
+      COMM_PERSIST_BPS * psm <= 220 * 1024) {
     e = raise_smem_limit((const void*)comm_persist_kernel<MP, KM, VEC>, psm);
     if (e != cudaSuccess) return e;
     comm_persist_kernel<MP, KM, VEC><<<pgrid, COMM_THREADS, psm, s>>>(p);
