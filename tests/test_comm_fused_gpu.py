@@ -59,18 +59,22 @@ def test_comm_forward_matches_module_oracle(B, N, D, m, topk):
 
 @pytest.mark.parametrize("B,N,D,m,topk", [
     (4096, 6, 64, 16, 2), (4096, 6, 64, 16, 0), (1000, 32, 36, 8, 3),
-    (3001, 17, 64, 32, 1)])
+    (3001, 17, 64, 32, 1), (700, 6, 33, 16, 0), (1500, 5, 20, 3, 2),
+    (600, 8, 64, 64, 4), (149, 9, 64, 16, 8)])
 def test_comm_forward_large_batches(B, N, D, m, topk):
-    """Batches above four blocks per SM take the persistent form (weights
-    staged once per block, x tiles double-buffered): every episode matches
-    the oracle, and a slice of the batch run on its own (one block per
-    episode) gives the same bits."""
+    """Batches of at least one episode per SM take the multi-episode tile
+    form (weights staged once per block, tiles of several episodes, a ragged
+    last tile): every sampled episode matches the oracle, and a slice of the
+    batch run on its own (one block per episode) gives the same bits. Covers
+    4-byte staging (odd input width), padded message columns (m=3) and
+    m=64."""
     from tarmac_b200 import ops
     x = torch.randn(B, N, D, generator=torch.Generator().manual_seed(B + N))
     w = [t.cuda() for t in _weights(D, m, seed=m + topk + 1)]
     xc = x.cuda()
     out = ops.comm_forward(xc, *w, topk)
     sel = np.sort(np.random.default_rng(B).choice(B, size=64, replace=False))
+    sel[-1] = B - 1                                   # the ragged last tile
     ref, q, k = oracle.comm_forward(x.numpy()[sel], *(t.cpu().numpy() for t in w),
                                     topk)
     ok = ~_near_tie_rows(q, k, topk)

@@ -27,8 +27,8 @@ namespace tarmac {
 
 constexpr int COMM_THREADS = 128;
 constexpr int COMM_XTILE = 32;  // x rows staged per step
-// resident blocks per SM of the persistent form for large batches
-constexpr int COMM_PERSIST_BPS = 8;
+// resident blocks per SM of the multi-episode tile form for large batches
+constexpr int COMM_TILE_BPS = 8;
 
 
 
@@ -349,52 +349,257 @@ __global__ void __launch_bounds__(COMM_THREADS, 1) comm_forward_kernel(CommParam
   comm_attend<MP, KM>(p, b, sq, sk, sv, sg, spw, spb);
 }
 
-// Persistent form for large batches of short episodes (N <= 32, W_qkv in
-// shared memory): a block stages the weights once and loops over episodes
-// b = blockIdx.x, blockIdx.x + gridDim.x, ...; the next episode's x rows are
-// copied into the second of two x tiles while the current episode is
-// projected and attended. Each episode's outputs are those of
-// comm_forward_kernel (same functions, same order of operations).
+// Multi-episode form for large batches of short episodes (N <= 32, W_qkv in
+// shared memory). A tile is E consecutive episodes (R = E * N <= RT rows,
+// contiguous in x); blocks loop over tiles with stride gridDim.x, the weights
+// staged once per block and the next tile's x rows copied in once the
+// current tile's projection has consumed them. Per tile:
+//   projection  thread (column c, row group g) forms q, k and v column c of
+//               four rows at a time (12 accumulators): every staged W_qkv
+//               piece feeds four rows, every x piece three outputs;
+//   scores      one thread per (agent, key) pair of an episode;
+//   selection   one thread per agent: the k best scores (lowest key index on
+//               a tie), normalised weights and key indices;
+//   aggregate   one thread per (agent, message column): V aggregate (top-k)
+//               or the online softmax (dense), then GELU;
+//   output      one thread per (agent, output column), W_proj staged
+//               transposed so consecutive threads read consecutive words.
+// Every output is formed with the operations of comm_forward_kernel in the
+// same order, so both forms give the same bits.
+template <int MP>
+__host__ __device__ constexpr int comm_tile_rows() {
+  return 4 * (COMM_THREADS / MP) > 32 ? 4 * (COMM_THREADS / MP) : 32;
+}
+
 template <int MP, int KM, bool VEC>
-__global__ void __launch_bounds__(COMM_THREADS, COMM_PERSIST_BPS) comm_persist_kernel(CommParams p) {
+__global__ void __launch_bounds__(COMM_THREADS, COMM_TILE_BPS)
+    comm_tile_kernel(CommParams p, int E) {
   extern __shared__ __align__(16) float comm_sm[];
-  const int N = p.N, D = p.in_dim, m = p.m;
+  constexpr int RG = COMM_THREADS / MP;  // row groups
+  constexpr int RT = comm_tile_rows<MP>();
+  constexpr int KS = KM > 0 ? KM : 1;
+  const int N = p.N, D = p.in_dim, m = p.m, M3 = 3 * m;
   const int DS = comm_row_stride(D, VEC);
-  const int M3 = 3 * m;
-  float* sq = comm_sm;
-  float* sk = sq + (size_t)N * MP;
-  float* sv = sk + (size_t)N * MP;
-  float* sx = sv + (size_t)N * MP;  // two tiles of N rows
-  float* sg = sx + (size_t)2 * N * DS;
-  float* sw = sg + COMM_THREADS;
-  float* spw = sw + (size_t)M3 * DS;
-  float* spb = spw + m * m;
+  float* sw = comm_sm;                    // [3m][DS]
+  float* sx = sw + (size_t)M3 * DS;       // [RT][DS]
+  float* sq = sx + (size_t)RT * DS;       // [RT][MP] each
+  float* sk = sq + RT * MP;
+  float* sv = sk + RT * MP;
+  float* sg = sv + RT * MP;               // GELU(message) [RT][MP]
+  float* swn = sg + RT * MP;              // normalised weights [RT][KS]
+  int* sidx = reinterpret_cast<int*>(swn + RT * KS);  // key indices [RT][KS]
+  float* ss = reinterpret_cast<float*>(sidx + RT * KS);  // scores [RT][N]
+  float* spt = ss + RT * N;               // W_proj transposed [m][m]
+  float* spb = spt + m * m;
   float* sbq = spb + m;
+  const int ntile = (p.B + E - 1) / E;
+
+  auto stage_tile = [&](int t) {
+    const int b0 = t * E;
+    const int R = min(E, p.B - b0) * N;
+    const float* src = p.x + (int64_t)b0 * N * D;
+    if constexpr (VEC) {
+      const int D4 = D >> 2;
+      for (int q = threadIdx.x; q < R * D4; q += COMM_THREADS) {
+        const int r = q / D4, c4 = q - r * D4;
+        cp_async16(sx + r * DS + 4 * c4, src + (int64_t)r * D + 4 * c4);
+      }
+    } else {
+      for (int q = threadIdx.x; q < R * D; q += COMM_THREADS) {
+        const int r = q / D, c = q - r * D;
+        cp_async4(sx + r * DS + c, src + q);
+      }
+    }
+  };
 
   comm_stage<VEC>(sw, DS, p.wqkv, M3, D);
-  for (int e = threadIdx.x; e < m * m; e += blockDim.x) cp_async4(spw + e, p.wproj + e);
-  for (int e = threadIdx.x; e < m; e += blockDim.x) cp_async4(spb + e, p.bproj + e);
-  for (int e = threadIdx.x; e < M3; e += blockDim.x) cp_async4(sbq + e, p.bqkv + e);
-  if (m < MP)
-    for (int e = threadIdx.x; e < 3 * N * MP; e += blockDim.x) sq[e] = 0.f;
-  int cur = 0;
-  if ((int)blockIdx.x < p.B)
-    comm_stage<VEC>(sx, DS, p.x + (int64_t)blockIdx.x * N * D, N, D);
-  for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
-    cp_async_wait_all();  // this episode's x rows (and, first, the weights)
+  for (int e = threadIdx.x; e < m * m; e += COMM_THREADS) {
+    const int oc = e / m, t = e - oc * m;
+    cp_async4(spt + t * m + oc, p.wproj + e);
+  }
+  for (int e = threadIdx.x; e < m; e += COMM_THREADS) cp_async4(spb + e, p.bproj + e);
+  for (int e = threadIdx.x; e < M3; e += COMM_THREADS) cp_async4(sbq + e, p.bqkv + e);
+  if (m < MP)  // padded message columns stay zero
+    for (int e = threadIdx.x; e < 3 * RT * MP; e += COMM_THREADS) sq[e] = 0.f;
+  if ((int)blockIdx.x < ntile) stage_tile(blockIdx.x);
+
+  const int pc = threadIdx.x % MP, pg = threadIdx.x / MP;
+  for (int tile = blockIdx.x; tile < ntile; tile += gridDim.x) {
+    const int b0 = tile * E;
+    const int R = min(E, p.B - b0) * N;
+    cp_async_wait_all();  // this tile's x rows (and, first, the weights)
     __syncthreads();
-    const int nb = b + gridDim.x;
-    if (nb < p.B)
-      comm_stage<VEC>(sx + (size_t)(cur ^ 1) * N * DS, DS,
-                      p.x + (int64_t)nb * N * D, N, D);
-    comm_project<MP, VEC>(p, sx + (size_t)cur * N * DS, DS, sw, sbq, 0, N,
-                          sq, sk, sv);
+
+    // ---- projection: four rows x (q, k, v) column pc per step -------------
+    if (pc < m) {
+      const float* w0 = sw + pc * DS;
+      const float* w1 = sw + (pc + m) * DS;
+      const float* w2 = sw + (pc + 2 * m) * DS;
+      for (int r0 = 4 * pg; r0 < R; r0 += 4 * RG) {
+        const float* x0 = sx + r0 * DS;
+        float a0[4] = {0.f, 0.f, 0.f, 0.f}, a1[4] = {0.f, 0.f, 0.f, 0.f},
+              a2[4] = {0.f, 0.f, 0.f, 0.f};
+        if constexpr (VEC) {
+          for (int c = 0; c < D; c += 4) {
+            const float4 u0 = *reinterpret_cast<const float4*>(w0 + c);
+            const float4 u1 = *reinterpret_cast<const float4*>(w1 + c);
+            const float4 u2 = *reinterpret_cast<const float4*>(w2 + c);
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const float4 xv = *reinterpret_cast<const float4*>(x0 + r * DS + c);
+              a0[r] = fmaf(xv.x, u0.x, a0[r]);
+              a0[r] = fmaf(xv.y, u0.y, a0[r]);
+              a0[r] = fmaf(xv.z, u0.z, a0[r]);
+              a0[r] = fmaf(xv.w, u0.w, a0[r]);
+              a1[r] = fmaf(xv.x, u1.x, a1[r]);
+              a1[r] = fmaf(xv.y, u1.y, a1[r]);
+              a1[r] = fmaf(xv.z, u1.z, a1[r]);
+              a1[r] = fmaf(xv.w, u1.w, a1[r]);
+              a2[r] = fmaf(xv.x, u2.x, a2[r]);
+              a2[r] = fmaf(xv.y, u2.y, a2[r]);
+              a2[r] = fmaf(xv.z, u2.z, a2[r]);
+              a2[r] = fmaf(xv.w, u2.w, a2[r]);
+            }
+          }
+        } else {
+          for (int c = 0; c < D; ++c) {
+            const float u0 = w0[c], u1 = w1[c], u2 = w2[c];
+#pragma unroll
+            for (int r = 0; r < 4; ++r) {
+              const float xv = x0[r * DS + c];
+              a0[r] = fmaf(xv, u0, a0[r]);
+              a1[r] = fmaf(xv, u1, a1[r]);
+              a2[r] = fmaf(xv, u2, a2[r]);
+            }
+          }
+        }
+        const float bq0 = sbq[pc], bq1 = sbq[pc + m], bq2 = sbq[pc + 2 * m];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          if (r0 + r < R) {
+            sq[(r0 + r) * MP + pc] = a0[r] + bq0;
+            sk[(r0 + r) * MP + pc] = a1[r] + bq1;
+            sv[(r0 + r) * MP + pc] = a2[r] + bq2;
+          }
+        }
+      }
+    }
+    __syncthreads();  // q, k, v complete; the x tile is free
+    if (tile + (int)gridDim.x < ntile) stage_tile(tile + gridDim.x);
+
+    // ---- scores: one thread per (agent, key) pair --------------------------
+    for (int it = threadIdx.x; it < R * N; it += COMM_THREADS) {
+      const int r = it / N, j = it - r * N;
+      const float* qr = sq + r * MP;
+      const float* kr = sk + (r - r % N + j) * MP;
+      float s = 0.f;
+#pragma unroll
+      for (int t = 0; t < MP; t += 4) {
+        const float4 a = *reinterpret_cast<const float4*>(qr + t);
+        const float4 f = *reinterpret_cast<const float4*>(kr + t);
+        s = fmaf(a.x, f.x, s);
+        s = fmaf(a.y, f.y, s);
+        s = fmaf(a.z, f.z, s);
+        s = fmaf(a.w, f.w, s);
+      }
+      ss[it] = KM > 0 ? s : s * p.scale;
+    }
     __syncthreads();
-    comm_attend<MP, KM>(p, b, sq, sk, sv, sg, spw, spb);
-    __syncthreads();  // q, k, v, the GELU buffer and this x tile are free
-    cur ^= 1;
+
+    // ---- selection: one thread per agent -----------------------------------
+    if constexpr (KM > 0) {
+      for (int r = threadIdx.x; r < R; r += COMM_THREADS) {
+        const int i = r % N;
+        const float* sr = ss + r * N;
+        float bs[KM];
+        int bi[KM];
+#pragma unroll
+        for (int s = 0; s < KM; ++s) {
+          bs[s] = -INFINITY;
+          bi[s] = -1;
+        }
+        for (int j = 0; j < N; ++j) {
+          const float s = sr[j];
+          if (j != i && s > bs[KM - 1]) buf_insert<KM, false>(bs, bi, s, j);
+        }
+        const int kk = p.topk;
+        const float mx = bs[0] * p.scale;
+        float den = 0.f, w[KM];
+#pragma unroll
+        for (int s = 0; s < KM; ++s) {
+          w[s] = (s < kk && bi[s] >= 0) ? expf(bs[s] * p.scale - mx) : 0.f;
+          den += w[s];
+        }
+#pragma unroll
+        for (int s = 0; s < KM; ++s) {
+          const bool on = w[s] > 0.f;
+          swn[r * KS + s] = on ? w[s] / den : 0.f;
+          sidx[r * KS + s] = on ? bi[s] : -1;
+        }
+      }
+      __syncthreads();
+    }
+
+    // ---- aggregate and GELU: one thread per (agent, message column) --------
+    for (int it = threadIdx.x; it < R * MP; it += COMM_THREADS) {
+      const int r = it / MP, c = it % MP;
+      const int r0 = r - r % N;  // the episode's first row
+      float msg = 0.f;
+      if constexpr (KM > 0) {
+#pragma unroll
+        for (int s = 0; s < KM; ++s) {
+          const int j = sidx[r * KS + s];
+          if (j >= 0) msg = fmaf(swn[r * KS + s], sv[(r0 + j) * MP + c], msg);
+        }
+      } else {
+        const int i = r - r0;
+        const float* sr = ss + r * N;
+        float mref = -INFINITY, l = 0.f;
+        for (int j = 0; j < N; ++j) {
+          if (j == i) continue;
+          const float s = sr[j];
+          if (s > mref) {
+            const float a = expf(mref - s);
+            l *= a;
+            msg *= a;
+            mref = s;
+          }
+          const float e = expf(s - mref);
+          l += e;
+          msg = fmaf(e, sv[(r0 + j) * MP + c], msg);
+        }
+        msg *= 1.0f / l;
+      }
+      sg[it] = gelu_erf(msg);
+    }
+    __syncthreads();
+
+    // ---- output projection: one thread per (agent, output column) ----------
+    float* out = p.out + (int64_t)b0 * N * m;
+    for (int it = threadIdx.x; it < R * m; it += COMM_THREADS) {
+      const int r = it / m, oc = it - r * m;
+      const float* gr = sg + r * MP;
+      float acc = 0.f;
+#pragma unroll
+      for (int t = 0; t < MP; ++t)
+        if (t < m) acc = fmaf(gr[t], spt[t * m + oc], acc);
+      out[it] = acc + spb[oc];
+    }
+    // the next iteration's first barrier keeps sg and ss until every thread
+    // is done with them
   }
   cp_async_wait_all();
+}
+
+// Dynamic shared memory of comm_tile_kernel (W_qkv included).
+template <int MP, int KM>
+static size_t comm_tile_smem_bytes(int N, int in_dim, int m, bool vec) {
+  constexpr int RT = comm_tile_rows<MP>();
+  const int KS = KM > 0 ? KM : 1;
+  const int DS = comm_row_stride(in_dim, vec);
+  return sizeof(float) * ((size_t)3 * m * DS + (size_t)RT * DS +
+                          (size_t)4 * RT * MP + (size_t)2 * RT * KS +
+                          (size_t)RT * N + (size_t)m * m + 4 * (size_t)m);
 }
 
 size_t comm_smem_bytes(int N, int in_dim, int m, int MP, bool vec) {
@@ -418,25 +623,24 @@ static cudaError_t launch_comm_t(CommParams p, cudaStream_t s) {
       sizeof(float) * (size_t)3 * p.m * comm_row_stride(p.in_dim, VEC);
   p.w_smem = sm + wb <= COMM_SMEM_WITH_W;
   if (p.w_smem) sm += wb;
-  // Large batches of short episodes: the persistent form stages the weights
-  // once per block instead of once per episode (B=4096, N=6: 41 us with one
-  // block per episode).
+  // Large batches of short episodes: the multi-episode tile form stages the
+  // weights once per block, shares each W_qkv read among four rows and forms
+  // each score once (B=4096, N=6: 41 us with one block per episode). Tiles
+  // of about B / (4 * SMs) episodes, at most COMM_TILE_BPS blocks per SM.
   int dev = 0, nsm = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   if (e != cudaSuccess) return e;
-  // at least two episodes per block, at most COMM_PERSIST_BPS blocks per SM
-  const int pgrid = std::min(COMM_PERSIST_BPS * nsm, p.B / 2);
-  const size_t psm = sizeof(float) * ((size_t)p.m * p.m + 4 * (size_t)p.m +
-                                      (size_t)3 * p.N * MP +
-                                      (size_t)2 * p.N * comm_row_stride(p.in_dim, VEC) +
-                                      COMM_THREADS) + wb;
-  if (p.w_smem && p.N <= COMM_XTILE && p.B >= 4 * nsm &&
-      COMM_PERSIST_BPS * psm <= 220 * 1024) {
-    e = raise_smem_limit((const void*)comm_persist_kernel<MP, KM, VEC>, psm);
+  constexpr int RT = comm_tile_rows<MP>();
+  const size_t tsm = comm_tile_smem_bytes<MP, KM>(p.N, p.in_dim, p.m, VEC);
+  if (p.N <= RT && p.B >= nsm && tsm <= 220 * 1024) {
+    const int bps = (int)std::min<size_t>(COMM_TILE_BPS, (220 * 1024) / tsm);
+    const int E = std::max(1, std::min(RT / p.N, (p.B + 4 * nsm - 1) / (4 * nsm)));
+    const int grid = std::min((p.B + E - 1) / E, bps * nsm);
+    e = raise_smem_limit((const void*)comm_tile_kernel<MP, KM, VEC>, tsm);
     if (e != cudaSuccess) return e;
-    comm_persist_kernel<MP, KM, VEC><<<pgrid, COMM_THREADS, psm, s>>>(p);
+    comm_tile_kernel<MP, KM, VEC><<<grid, COMM_THREADS, tsm, s>>>(p, E);
     return cudaGetLastError();
   }
   e = raise_smem_limit(
