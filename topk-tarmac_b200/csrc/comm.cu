@@ -349,6 +349,35 @@ __global__ void __launch_bounds__(COMM_THREADS, 1) comm_forward_kernel(CommParam
   comm_attend<MP, KM>(p, b, sq, sk, sv, sg, spw, spb);
 }
 
+// q / n through one float multiply, for 0 <= q, 1 <= n and q + n < 2^22:
+// (q + 0.5) / n lies at least 0.5 / n from an integer and the rounded
+// product (inv_n = 1/n rounded) is within (q + n) 2^-23 / n of it, so
+// truncation gives the exact quotient.
+__device__ __forceinline__ int small_div(int q, float inv_n) {
+  return __float2int_rz((static_cast<float>(q) + 0.5f) * inv_n);
+}
+
+// Copy R contiguous rows of D floats into shared rows of DS floats, the
+// 16-byte pieces (VEC) or words dealt over all threads in order.
+template <bool VEC>
+__device__ __forceinline__ void comm_stage_flat(float* dst, int DS,
+                                                const float* src, int R, int D) {
+  if constexpr (VEC) {
+    const int D4 = D >> 2;
+    const float inv = 1.0f / D4;
+    for (int q = threadIdx.x; q < R * D4; q += blockDim.x) {
+      const int r = small_div(q, inv), c4 = q - r * D4;
+      cp_async16(dst + r * DS + 4 * c4, src + 4 * (int64_t)q);
+    }
+  } else {
+    const float inv = 1.0f / D;
+    for (int q = threadIdx.x; q < R * D; q += blockDim.x) {
+      const int r = small_div(q, inv), c = q - r * D;
+      cp_async4(dst + r * DS + c, src + q);
+    }
+  }
+}
+
 // Multi-episode form for large batches of short episodes (N <= 32, W_qkv in
 // shared memory). A tile is E consecutive episodes (R = E * N <= RT rows,
 // contiguous in x); blocks loop over tiles with stride gridDim.x, the weights
@@ -360,10 +389,13 @@ __global__ void __launch_bounds__(COMM_THREADS, 1) comm_forward_kernel(CommParam
 //   scores      one thread per (agent, key) pair of an episode;
 //   selection   one thread per agent: the k best scores (lowest key index on
 //               a tie), normalised weights and key indices;
-//   aggregate   one thread per (agent, message column): V aggregate (top-k)
-//               or the online softmax (dense), then GELU;
-//   output      one thread per (agent, output column), W_proj staged
-//               transposed so consecutive threads read consecutive words.
+//   aggregate   thread (message column c, row group g) over rows g, g + RG,
+//               ...: V aggregate (top-k) or the online softmax (dense), GELU;
+//   output      thread (output column c, row group g), four rows per step,
+//               W_proj column c in registers (m <= 16) or read from a
+//               transposed copy (consecutive threads, consecutive words).
+// Row and column indices come from small_div (one float multiply) instead of
+// integer division by the runtime N, m and in_dim.
 // Every output is formed with the operations of comm_forward_kernel in the
 // same order, so both forms give the same bits.
 template <int MP>
@@ -394,27 +426,17 @@ __global__ void __launch_bounds__(COMM_THREADS, COMM_TILE_BPS)
   float* sbq = spb + m;
   const int ntile = (p.B + E - 1) / E;
 
+  const float inv_n = 1.0f / N;
   auto stage_tile = [&](int t) {
     const int b0 = t * E;
     const int R = min(E, p.B - b0) * N;
-    const float* src = p.x + (int64_t)b0 * N * D;
-    if constexpr (VEC) {
-      const int D4 = D >> 2;
-      for (int q = threadIdx.x; q < R * D4; q += COMM_THREADS) {
-        const int r = q / D4, c4 = q - r * D4;
-        cp_async16(sx + r * DS + 4 * c4, src + (int64_t)r * D + 4 * c4);
-      }
-    } else {
-      for (int q = threadIdx.x; q < R * D; q += COMM_THREADS) {
-        const int r = q / D, c = q - r * D;
-        cp_async4(sx + r * DS + c, src + q);
-      }
-    }
+    comm_stage_flat<VEC>(sx, DS, p.x + (int64_t)b0 * N * D, R, D);
   };
 
-  comm_stage<VEC>(sw, DS, p.wqkv, M3, D);
+  comm_stage_flat<VEC>(sw, DS, p.wqkv, M3, D);
+  const float inv_m = 1.0f / m;
   for (int e = threadIdx.x; e < m * m; e += COMM_THREADS) {
-    const int oc = e / m, t = e - oc * m;
+    const int oc = small_div(e, inv_m), t = e - oc * m;
     cp_async4(spt + t * m + oc, p.wproj + e);
   }
   for (int e = threadIdx.x; e < m; e += COMM_THREADS) cp_async4(spb + e, p.bproj + e);
@@ -489,9 +511,9 @@ __global__ void __launch_bounds__(COMM_THREADS, COMM_TILE_BPS)
 
     // ---- scores: one thread per (agent, key) pair --------------------------
     for (int it = threadIdx.x; it < R * N; it += COMM_THREADS) {
-      const int r = it / N, j = it - r * N;
+      const int r = small_div(it, inv_n), j = it - r * N;
       const float* qr = sq + r * MP;
-      const float* kr = sk + (r - r % N + j) * MP;
+      const float* kr = sk + (small_div(r, inv_n) * N + j) * MP;
       float s = 0.f;
 #pragma unroll
       for (int t = 0; t < MP; t += 4) {
@@ -509,7 +531,7 @@ __global__ void __launch_bounds__(COMM_THREADS, COMM_TILE_BPS)
     // ---- selection: one thread per agent -----------------------------------
     if constexpr (KM > 0) {
       for (int r = threadIdx.x; r < R; r += COMM_THREADS) {
-        const int i = r % N;
+        const int i = r - small_div(r, inv_n) * N;
         const float* sr = ss + r * N;
         float bs[KM];
         int bi[KM];
@@ -540,50 +562,74 @@ __global__ void __launch_bounds__(COMM_THREADS, COMM_TILE_BPS)
       __syncthreads();
     }
 
-    // ---- aggregate and GELU: one thread per (agent, message column) --------
-    for (int it = threadIdx.x; it < R * MP; it += COMM_THREADS) {
-      const int r = it / MP, c = it % MP;
-      const int r0 = r - r % N;  // the episode's first row
-      float msg = 0.f;
-      if constexpr (KM > 0) {
+    // ---- aggregate and GELU: thread (column pc, row group pg) ---------------
+    if (pc < m) {
+      for (int r = pg; r < R; r += RG) {
+        const int r0 = small_div(r, inv_n) * N;  // the episode's first row
+        float msg = 0.f;
+        if constexpr (KM > 0) {
 #pragma unroll
-        for (int s = 0; s < KM; ++s) {
-          const int j = sidx[r * KS + s];
-          if (j >= 0) msg = fmaf(swn[r * KS + s], sv[(r0 + j) * MP + c], msg);
-        }
-      } else {
-        const int i = r - r0;
-        const float* sr = ss + r * N;
-        float mref = -INFINITY, l = 0.f;
-        for (int j = 0; j < N; ++j) {
-          if (j == i) continue;
-          const float s = sr[j];
-          if (s > mref) {
-            const float a = expf(mref - s);
-            l *= a;
-            msg *= a;
-            mref = s;
+          for (int s = 0; s < KM; ++s) {
+            const int j = sidx[r * KS + s];
+            if (j >= 0) msg = fmaf(swn[r * KS + s], sv[(r0 + j) * MP + pc], msg);
           }
-          const float e = expf(s - mref);
-          l += e;
-          msg = fmaf(e, sv[(r0 + j) * MP + c], msg);
+        } else {
+          const int i = r - r0;
+          const float* sr = ss + r * N;
+          float mref = -INFINITY, l = 0.f;
+          for (int j = 0; j < N; ++j) {
+            if (j == i) continue;
+            const float s = sr[j];
+            if (s > mref) {
+              const float a = expf(mref - s);
+              l *= a;
+              msg *= a;
+              mref = s;
+            }
+            const float e = expf(s - mref);
+            l += e;
+            msg = fmaf(e, sv[(r0 + j) * MP + pc], msg);
+          }
+          msg *= 1.0f / l;
         }
-        msg *= 1.0f / l;
+        sg[r * MP + pc] = gelu_erf(msg);
       }
-      sg[it] = gelu_erf(msg);
     }
     __syncthreads();
 
-    // ---- output projection: one thread per (agent, output column) ----------
-    float* out = p.out + (int64_t)b0 * N * m;
-    for (int it = threadIdx.x; it < R * m; it += COMM_THREADS) {
-      const int r = it / m, oc = it - r * m;
-      const float* gr = sg + r * MP;
-      float acc = 0.f;
+    // ---- output projection: thread (column pc, row group pg), four rows ----
+    // per step; W_proj column pc from registers (m <= 16) or shared memory
+    if (pc < m) {
+      float wc[MP <= 16 ? MP : 1];
+      if constexpr (MP <= 16) {
 #pragma unroll
-      for (int t = 0; t < MP; ++t)
-        if (t < m) acc = fmaf(gr[t], spt[t * m + oc], acc);
-      out[it] = acc + spb[oc];
+        for (int t = 0; t < MP; ++t) wc[t] = t < m ? spt[t * m + pc] : 0.f;
+      }
+      const float bo = spb[pc];
+      float* out = p.out + (int64_t)b0 * N * m;
+      for (int r0 = 4 * pg; r0 < R; r0 += 4 * RG) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 4
+        for (int t = 0; t < MP; t += 4) {
+          float w4[4];
+#pragma unroll
+          for (int u = 0; u < 4; ++u) {
+            if constexpr (MP <= 16) w4[u] = wc[t + u];
+            else w4[u] = t + u < m ? spt[(t + u) * m + pc] : 0.f;
+          }
+#pragma unroll
+          for (int rr = 0; rr < 4; ++rr) {
+            const float4 gv = *reinterpret_cast<const float4*>(sg + (r0 + rr) * MP + t);
+            if (t < m) acc[rr] = fmaf(gv.x, w4[0], acc[rr]);
+            if (t + 1 < m) acc[rr] = fmaf(gv.y, w4[1], acc[rr]);
+            if (t + 2 < m) acc[rr] = fmaf(gv.z, w4[2], acc[rr]);
+            if (t + 3 < m) acc[rr] = fmaf(gv.w, w4[3], acc[rr]);
+          }
+        }
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr)
+          if (r0 + rr < R) out[(r0 + rr) * m + pc] = acc[rr] + bo;
+      }
     }
     // the next iteration's first barrier keeps sg and ss until every thread
     // is done with them
