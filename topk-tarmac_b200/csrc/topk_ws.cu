@@ -40,7 +40,7 @@ constexpr int WS_KWARP0 = WS_CONSUMERS / 32;
 constexpr int WS_QWARP = WS_KWARP0 + WS_KPROD / 32;
 constexpr int WS_MMA_WARP = WS_QWARP + 1;
 constexpr int WS_THREADS = (WS_MMA_WARP + 1) * 32;
-constexpr int WS_NS = 2;                 // K ring slots
+constexpr int WS_NS = 3;                 // K ring slots
 constexpr int WS_RK = 128;               // keys per K tile
 constexpr int WS_NQ = 4;                 // query tiles per episode (max)
 constexpr int WS_MAX_N = WS_NQ * 128;
@@ -150,15 +150,25 @@ struct WsPlan {
   static constexpr int RAWBYTES = F32 ? 2 * WS_NR * WS_RAWB : 0;
   static constexpr int SVBYTES = WS_MAX_N * (KC * CH + 4) * 4;
   static constexpr int VROW = DP * (int)sizeof(T);
+  // staged V rows: 16-byte piece c of row r sits at piece c ^ vswz(r) of the
+  // row, so the pieces that the epilogue's 32 lanes read from 32 random rows
+  // spread over all eight 16-byte bank groups (unswizzled, piece c of every
+  // 64-byte row falls in one of two)
+  static constexpr int VPPR = VROW / 16;                 // pieces per row
+  static constexpr int VRPB = VPPR < 8 ? 8 / VPPR : 1;   // rows per 128 bytes
+  __device__ static __forceinline__ int vswz(int r) { return (r / VRPB) & (VPPR - 1); }
   static constexpr int VALL = WS_MAX_N * VROW;
   static constexpr int REST = KBYTES + RAWBYTES + SVBYTES;
   static constexpr int LIM = (int)WS_SMEM_LIMIT;
   // preference: Q double buffered (the next episode's Q is ready when the
   // current one ends; with one buffer the products wait for it at every
-  // episode boundary: bf16 d = 64 measured 549 against 319 us), then V
-  // staged (the epilogue reads shared memory instead of gathering from L2)
+  // episode boundary: bf16 d = 64 measured 549 against 319 us), then, for
+  // bf16, V staged (the epilogue reads shared memory instead of gathering
+  // from L2: d = 32 265 against 269 us). fp32 gathers from L2: its raw rings
+  // and split stores already load the shared-memory pipe, which the tensor
+  // core's operand reads take first (C2 k = 2 84.8 against 87.4 us).
   static constexpr int NQB = (REST + 2 * WS_NQ * QTILE <= LIM) ? 2 : 1;
-  static constexpr bool VST = REST + NQB * WS_NQ * QTILE + VALL <= LIM;
+  static constexpr bool VST = !F32 && REST + NQB * WS_NQ * QTILE + VALL <= LIM;
   static constexpr int QBYTES = NQB * WS_NQ * QTILE;
   static constexpr int VBYTES = VST ? VALL : 0;
   static constexpr int TOTAL = QBYTES + REST + VBYTES;
@@ -251,7 +261,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
       for (int e = tid; e < N * PPR; e += WS_KPROD) {
         const int r = e / PPR, c = e - (e / PPR) * PPR;
         const bool ok = c * EPP < d;
-        ws::cp16(va + (uint32_t)e * 16u, ok ? V + (int64_t)r * p.st.vn + c * EPP : V, ok);
+        ws::cp16(va + (uint32_t)(r * PPR + (c ^ Plan::vswz(r))) * 16u,
+                 ok ? V + (int64_t)r * p.st.vn + c * EPP : V, ok);
       }
       asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(
                        tc::smem_addr(&sh.vfull))
@@ -291,30 +302,32 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
         if (Plan::VST && w == ipe - 1 && !stage_v(it)) break;
       }
     } else {
-      // one K tile at a time straight into the ring, announced once its
-      // copies have landed (the tile's rows were prefetched into L2 an
-      // episode earlier)
-      uint32_t kc = 0;
-      bool live = true;
-      for (int it = 0; it < nep && live; ++it) {
-        if (it + 1 < nep) prefetch(it + 1);
-        for (int j = 0; j < nkt; ++j, ++kc) {
-          const int s = kc % WS_NS;
-          if (!ws::wait(&sh.kempty[s], ((kc / WS_NS) & 1) ^ 1, abort_flag)) {
-            live = false;
-            break;
-          }
+      // K tiles straight into the ring, one tile in flight ahead: tile n's
+      // copies are issued before the producers wait for tile n - 1's to land
+      // and announce it (the rows were prefetched into L2 an episode earlier)
+      const int total = nep * nkt;
+      for (int n = 0; n <= total; ++n) {
+        if (n < total) {
+          const int it = n / nkt, j = n - it * nkt;
+          if (j == 0 && it + 1 < nep) prefetch(it + 1);
+          const int s = n % WS_NS;
+          if (!ws::wait(&sh.kempty[s], ((n / WS_NS) & 1) ^ 1, abort_flag)) break;
           ws::copy_tile_bf16<DP, WS_RK, WS_KPROD>(
               ka + (uint32_t)(s * KTILE),
               reinterpret_cast<const __nv_bfloat16*>(kptr(it, WS_RK * j)), p.st.kn,
               N - WS_RK * j, d, tid);
           asm volatile("cp.async.commit_group;" ::: "memory");
+          asm volatile("cp.async.wait_group 1;" ::: "memory");
+        } else {
           asm volatile("cp.async.wait_group 0;" ::: "memory");
+        }
+        if (n > 0) {
+          const int pn = n - 1, pit = pn / nkt;
           tc::fence_async_smem();
           __syncwarp();
-          if (lane == 0) ws::arrive(&sh.kfull[s]);
+          if (lane == 0) ws::arrive(&sh.kfull[pn % WS_NS]);
+          if (Plan::VST && pn - pit * nkt == nkt - 1 && !stage_v(pit)) break;
         }
-        if (live && Plan::VST && !stage_v(it)) live = false;
       }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
@@ -609,7 +622,8 @@ __global__ void __launch_bounds__(WS_THREADS, 1)
 #pragma unroll
           for (int m = 0; m < KC; ++m) {
             if (m < kk && !empty) {
-              const uint4 raw = reinterpret_cast<const uint4*>(sV + bi[m] * DP)[c];
+              const uint4 raw =
+                  reinterpret_cast<const uint4*>(sV + bi[m] * DP)[c ^ Plan::vswz(bi[m])];
               const uint32_t h[4] = {raw.x, raw.y, raw.z, raw.w};
               float f[EPV];
               if constexpr (F32) {
