@@ -43,6 +43,14 @@ SEED = 1234 + 7 * N_AGENTS + HEAD_D  # the reference's sweep seed
 # the reference's published fused top-k at this config (RTX PRO 6000, sm_120,
 # results/attention_core_batch.json): 837.7 us per step
 REF_PUBLISHED_US = 837.7
+# DRAM bytes (read + write) of one launch of the headline kernel
+# (topk_ws_kernel<float,16,2,8,0>, this workload) from an ncu capture with
+# cold caches: 100.8 MB read + 10.2 MB written. Replaced by --traffic when
+# given; recapture when the kernel changes.
+TRAFFIC_CAPTURED_BYTES = 111.0e6
+TRAFFIC_CAPTURED_NOTE = ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                         "launch of this kernel at this workload, cold caches "
+                         "(summary committed as profiles/topk_ws_f32_c2.md)")
 
 
 def log(*a) -> None:
@@ -696,21 +704,26 @@ def run_ours(args) -> int:
                 "us_per_step": 1e3 * ems},
         # The kernel's compute roof is the tensor pipe (every fp32 score is
         # six exact bf16 plane products); HBM is far from binding (AI of the
-        # fp32 top-k is N/8 flop/B). What binds in practice is the issue rate
-        # of the selection scan (ALU), which no roof here measures.
+        # fp32 top-k is N/8 flop/B). What binds in practice is the consumers'
+        # selection scan: its ALU issue and dependency chain, and its
+        # shared-memory accesses, which wait while the products' operand
+        # reads hold the shared-memory pipe. No roof here measures that.
         "roofline": {"bound": "tensor", "achieved": achieved_tc,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved_tc / peaks["bf16_tflops"],
                      "flops_per_launch": tc_flops,
-                     "traffic": args.traffic,
+                     "traffic": (args.traffic if args.traffic
+                                 else TRAFFIC_CAPTURED_BYTES),
                      "traffic_note": ("ncu dram bytes of one launch, given "
                                       "with --traffic" if args.traffic
-                                      else "not measured in this run"),
+                                      else TRAFFIC_CAPTURED_NOTE),
                      "peak_src": f"{peaks['src']}: bf16 GEMM burst",
                      "note": "bf16 tensor flops the kernel executes: six "
                              "plane products (exact hi/mid/lo split of the "
                              "fp32 q and k) per score",
-                     "binding": "ALU issue of the selection scan"},
+                     "binding": ("the selection scan: ALU issue and its "
+                                 "dependency chain, shared-memory accesses "
+                                 "held behind the products' operand reads")},
         "roofline_hbm": {"bound": "hbm", "achieved": achieved_gbs,
                          "peak": peaks["hbm_gbs"], "unit": "GB/s",
                          "frac": achieved_gbs / peaks["hbm_gbs"],
