@@ -18,6 +18,9 @@
 // sorted k-best buffer (top-k) or a base-2 online softmax (dense), the V
 // aggregate, GELU and the output projection. Sized for the reference's
 // MAPPO shapes (N up to 1024, msg_dim up to 64, in_dim up to 256).
+// Batches of at least one episode per SM with short episodes take the
+// multi-episode tile form (comm_tile_kernel below), which returns the same
+// bits.
 #include <algorithm>
 
 #include "comm.cuh"
