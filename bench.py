@@ -517,6 +517,12 @@ def run_ours(args) -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     multi = shard.init("nccl", timeout_s=300)
+    if multi:
+        # each rank's pinned host buffers on its own GPU's NUMA node (one
+        # rank keeps every host CPU for its CPU baseline)
+        cpus = shard.bind_to_gpu_cpus(dev)
+        if cpus:
+            log(f"rank {rank}: bound to {len(cpus)} CPUs local to its GPU")
 
     B, N, d, k = B_PER_GPU, N_AGENTS, HEAD_D, TOPK
     g = torch.Generator().manual_seed(SEED + 7919 * rank)

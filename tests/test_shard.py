@@ -89,3 +89,35 @@ def test_failed_rank_surfaces_as_error_on_peer():
     status = {r[0]: r[1] for r in res}
     assert status[1] == "error"
     assert status[0] == "error"  # its barrier fails (peer gone / timeout)
+
+
+class _FakeNvml:
+    """NVML stand-in: the GPU at bus id 0000001B:00 is local to CPUs 0-3 and
+    64; everything else is unknown."""
+
+    def __init__(self):
+        self.shutdown = False
+
+    def nvmlInit(self):
+        pass
+
+    def nvmlShutdown(self):
+        self.shutdown = True
+
+    def nvmlDeviceGetHandleByPciBusId(self, bus):
+        if not bus.endswith(":1B:00.0"):
+            raise RuntimeError("not found")
+        return "h"
+
+    def nvmlDeviceGetCpuAffinity(self, h, words):
+        return [0b1111, 0b1] + [0] * (words - 2)
+
+
+def test_local_cpus_reads_nvml_mask_within_current_affinity():
+    fake = _FakeNvml()
+    allowed = set(os.sched_getaffinity(0))
+    cpus = shard.local_cpus("00000000:1B:00.0", nvml=fake)
+    want = sorted({0, 1, 2, 3, 64} & allowed)
+    assert cpus == (want or None)
+    assert fake.shutdown
+    assert shard.local_cpus("00000000:2C:00.0", nvml=_FakeNvml()) is None

@@ -36,6 +36,49 @@ def env_world() -> tuple[int, int, int]:
             int(os.environ.get("WORLD_SIZE", "1")))
 
 
+def local_cpus(pci_bus_id: str, nvml=None) -> list[int] | None:
+    """The host CPUs NVML reports as local to the GPU at ``pci_bus_id``
+    (its NUMA node), intersected with this process's current affinity; None
+    when NVML is unavailable or reports nothing usable. Reads only."""
+    try:
+        if nvml is None:
+            import pynvml as nvml  # nvidia-ml-py
+        nvml.nvmlInit()
+    except Exception:
+        return None
+    try:
+        h = nvml.nvmlDeviceGetHandleByPciBusId(pci_bus_id)
+        words = 64  # 64-bit words: 4096 CPUs
+        mask = nvml.nvmlDeviceGetCpuAffinity(h, words)
+        cpus = {64 * w + b for w, m in enumerate(mask) for b in range(64) if (int(m) >> b) & 1}
+    except Exception:
+        return None
+    finally:
+        try:
+            nvml.nvmlShutdown()
+        except Exception:
+            pass
+    cpus &= set(os.sched_getaffinity(0))
+    return sorted(cpus) or None
+
+
+def bind_to_gpu_cpus(device: torch.device, nvml=None) -> list[int] | None:
+    """Restrict this process (one rank) to the host CPUs local to its GPU, so
+    its pinned host buffers are allocated and copied from that GPU's NUMA
+    node. Changes only this process's CPU affinity; returns the CPU list, or
+    None when it left the affinity unchanged."""
+    props = torch.cuda.get_device_properties(device)
+    bus = getattr(props, "pci_bus_id", None)
+    if bus is None:
+        return None
+    dom = getattr(props, "pci_domain_id", 0)
+    dev_id = getattr(props, "pci_device_id", 0)
+    cpus = local_cpus(f"{dom:08X}:{bus:02X}:{dev_id:02X}.0", nvml)
+    if cpus:
+        os.sched_setaffinity(0, cpus)
+    return cpus
+
+
 def init(backend: str, timeout_s: float = 120.0) -> bool:
     """Initialise the default process group from the environment when more
     than one rank runs; returns whether a group exists. A short timeout makes
