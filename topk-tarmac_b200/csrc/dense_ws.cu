@@ -45,7 +45,7 @@ constexpr int DWS_KEYS = 64;           // keys per tile
 constexpr int DWS_NQ = 4;              // query tiles per episode (max)
 constexpr int DWS_MAX_N = DWS_NQ * 128;
 constexpr int DWS_MIN_B = 4 * 148;     // at least four episodes per SM
-constexpr int DWS_SMEM_LIMIT = 230 * 1024;
+constexpr int DWS_SMEM_LIMIT = 227 * 1024;  // the per-block maximum (232,448 bytes)
 constexpr float DWS_LOG2E = 1.4426950408889634f;
 constexpr float DWS_RESCALE_LOG2 = 8.0f;
 

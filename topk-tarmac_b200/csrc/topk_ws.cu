@@ -46,7 +46,7 @@ constexpr int WS_NQ = 4;                 // query tiles per episode (max)
 constexpr int WS_MAX_N = WS_NQ * 128;
 constexpr int WS_NR = 4;                 // fp32 raw slots per producer ring
 constexpr int WS_RAWB = 64 * 16 * 4;     // one raw slot: 64 fp32 rows of 16
-constexpr size_t WS_SMEM_LIMIT = 230 * 1024;
+constexpr size_t WS_SMEM_LIMIT = 227 * 1024;  // the per-block maximum (232,448 bytes)
 
 namespace ws {
 
