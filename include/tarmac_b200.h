@@ -289,6 +289,22 @@ int tarmac_dense_attention_backward_noalloc(
     const void *dout, const int64_t *strides, int B, int N, int d, int dtype,
     float scale, float *dq, float *dk, float *dv, void *stream);
 
+/* Which kernel, and with which tiling, a call with these arguments would
+ * take — host-only: no launch, no device access, callable without a GPU.
+ * Replaces the tuned-configuration lookup of the reference
+ * (src/kernels/streaming_topk_attention.py:186-203 `_tuned_cfg`, and
+ * scripts/bench_attention_core.py:120-145 for the dense tilings): there the
+ * launch tiles come from a searched table; here the library chooses the
+ * kernel and its tiles from the shape, and this call reports that choice.
+ * op: 0 dense (tarmac_dense_attention), 1 top-k (tarmac_topk_attention, with
+ * `mode`), 2 streaming top-k (tarmac_streaming_topk_attention). Pointers are
+ * assumed on a 256-byte grid; strides as for those calls (NULL: contiguous).
+ * Writes a NUL-terminated JSON object of at most `len` bytes, e.g.
+ * {"kernel": "topk_ws", "query_tile": 128, "key_tile": 128, "chunk": 8,
+ * "chunks_kept": 2}. Status codes as those calls' argument checks. */
+int tarmac_kernel_plan(int op, int B, int N, int d, int dtype, int topk,
+                       int mode, const int64_t *strides, char *out, int len);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

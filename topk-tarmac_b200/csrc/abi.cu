@@ -4,6 +4,8 @@
 // kernel for the (mode, k, N, d, dtype) combination and launches it on the
 // caller's stream. No memory is allocated and no stream is synchronised.
 #include <math.h>
+#include <stdio.h>
+#include <string.h>
 
 #include <array>
 #include <mutex>
@@ -74,30 +76,40 @@ cudaError_t launch_topk_ws(const AttnParams& p, int dtype, bool tie_high,
 // one or two lanes per query row (topk_small.cu); otherwise the chunked
 // FFMA kernel when the episode's keys fit its shared memory, else the
 // streaming kernel.
-static cudaError_t launch_topk_small_k(const AttnParams& p, int dtype,
-                                       bool tie_high, cudaStream_t s) {
-  if (topk_ws_supported(p, dtype) &&
-      (dtype == TARMAC_BF16 ? topk_tc_supported(p) : topk_tc_f32_supported(p)))
-    return launch_topk_ws(p, dtype, tie_high, s);
-  if (dtype == TARMAC_BF16 && topk_tc_supported(p))
-    return launch_topk_tc(p, tie_high, s);
-  if (dtype == TARMAC_F32 && topk_tc_f32_supported(p))
-    return launch_topk_tc_f32(p, tie_high, s);
+enum TopkPlan { TOPK_WS, TOPK_TC, TOPK_SMALL, TOPK_CHUNK, TOPK_STREAM };
+static TopkPlan topk_plan(const AttnParams& p, int dtype) {
+  const bool tc = dtype == TARMAC_BF16 ? topk_tc_supported(p) : topk_tc_f32_supported(p);
+  if (tc && topk_ws_supported(p, dtype)) return TOPK_WS;
+  if (tc) return TOPK_TC;
   // short episodes the tensor-core kernel does not take: one or two lanes
   // per query row, several episodes per block
-  if (topk_small_supported(p)) return launch_topk_small(p, dtype, tie_high, s);
-  if (chunk_fits(p.N, p.d, p.topk)) {
-    if (dtype == TARMAC_BF16)
-      return tie_high ? launch_topk_chunk_bf16_high(p, s)
-                      : launch_topk_chunk_bf16_low(p, s);
-    return tie_high ? launch_topk_chunk_f32_high(p, s)
-                    : launch_topk_chunk_f32_low(p, s);
+  if (topk_small_supported(p)) return TOPK_SMALL;
+  if (chunk_fits(p.N, p.d, p.topk)) return TOPK_CHUNK;
+  return TOPK_STREAM;
+}
+
+static cudaError_t launch_topk_small_k(const AttnParams& p, int dtype,
+                                       bool tie_high, cudaStream_t s) {
+  switch (topk_plan(p, dtype)) {
+    case TOPK_WS: return launch_topk_ws(p, dtype, tie_high, s);
+    case TOPK_TC:
+      return dtype == TARMAC_BF16 ? launch_topk_tc(p, tie_high, s)
+                                  : launch_topk_tc_f32(p, tie_high, s);
+    case TOPK_SMALL: return launch_topk_small(p, dtype, tie_high, s);
+    case TOPK_CHUNK:
+      if (dtype == TARMAC_BF16)
+        return tie_high ? launch_topk_chunk_bf16_high(p, s)
+                        : launch_topk_chunk_bf16_low(p, s);
+      return tie_high ? launch_topk_chunk_f32_high(p, s)
+                      : launch_topk_chunk_f32_low(p, s);
+    default:
+      return dtype == TARMAC_BF16 ? launch_topk_stream_bf16(p, tie_high, s)
+                                  : launch_topk_stream_f32(p, tie_high, s);
   }
-  return dtype == TARMAC_BF16 ? launch_topk_stream_bf16(p, tie_high, s)
-                              : launch_topk_stream_f32(p, tie_high, s);
 }
 cudaError_t launch_topk_rows(const AttnParams& p, int dtype, cudaStream_t s);
 cudaError_t launch_dense(const AttnParams& p, int dtype, cudaStream_t s);
+int dense_plan(const AttnParams& p, int dtype);
 cudaError_t launch_prescore(const AttnParams& p, int dtype, const void* idx,
                             bool idx_i64, int kk, cudaStream_t s);
 cudaError_t launch_morton_code(const float* pos, int B, int N, int bits,
@@ -235,6 +247,70 @@ using namespace tarmac;
 extern "C" {
 
 int tarmac_abi_version(void) { return TARMAC_ABI_VERSION; }
+
+int tarmac_kernel_plan(int op, int B, int N, int d, int dtype, int topk,
+                       int mode, const int64_t* strides, char* out, int len) {
+  if (!out || len < 1) return TARMAC_ERR_NULL;
+  out[0] = '\0';
+  // planning reads shapes, strides and pointer alignment only: stand-in
+  // pointers on a 256-byte grid, as torch's allocator returns
+  const void* a = reinterpret_cast<const void*>((uintptr_t)1 << 20);
+  AttnParams p;
+  int st = fill_params(p, a, a, a, const_cast<void*>(a), strides, B, N, d, dtype, 1.0f);
+  if (st != TARMAC_OK) return st;
+  char buf[256];
+  if (op == 0) {  // dense
+    static const char* names[4] = {"dense_ws", "dense_tc", "dense_tc_f32", "dense_ffma"};
+    const int pl = dense_plan(p, dtype);
+    if (pl < 3)
+      snprintf(buf, sizeof buf,
+               "{\"kernel\": \"%s\", \"query_tile\": 128, \"key_tile\": 64}", names[pl]);
+    else
+      snprintf(buf, sizeof buf, "{\"kernel\": \"%s\"}", names[pl]);
+  } else if (op == 1 || op == 2) {  // top-k, streaming top-k
+    if (op == 2) mode = TARMAC_SELECT_ARGMAX;
+    if (mode != TARMAC_SELECT_ARGMAX && mode != TARMAC_SELECT_THRESHOLD &&
+        mode != TARMAC_SELECT_SORT)
+      return TARMAC_ERR_MODE;
+    if (topk < 1 || topk > N - 1 || (op == 2 && topk > STREAM_MAX_K)) return TARMAC_ERR_TOPK;
+    p.topk = topk;
+    p.mode = mode;
+    const bool reg = mode != TARMAC_SELECT_THRESHOLD && topk <= REGISTER_MAX_K;
+    if (!reg) {
+      snprintf(buf, sizeof buf, "{\"kernel\": \"topk_rows\"}");
+    } else {
+      const int kc = chunk_slots(topk);
+      switch (topk_plan(p, dtype)) {
+        case TOPK_WS:
+          snprintf(buf, sizeof buf,
+                   "{\"kernel\": \"topk_ws\", \"query_tile\": 128, \"key_tile\": 128, "
+                   "\"chunk\": 8, \"chunks_kept\": %d}", kc);
+          break;
+        case TOPK_TC:
+          snprintf(buf, sizeof buf,
+                   "{\"kernel\": \"topk_tc\", \"query_tile\": 128, \"key_tile\": %d, "
+                   "\"chunk\": 8, \"chunks_kept\": %d}",
+                   (dtype == TARMAC_F32 || d <= 16) ? 128 : 64, kc);
+          break;
+        case TOPK_SMALL:
+          snprintf(buf, sizeof buf, "{\"kernel\": \"topk_small\", \"lanes_per_row\": %d}",
+                   N <= 64 ? 2 : 1);
+          break;
+        case TOPK_CHUNK:
+          snprintf(buf, sizeof buf, "{\"kernel\": \"topk_chunk\", \"chunks_kept\": %d}", kc);
+          break;
+        default:
+          snprintf(buf, sizeof buf, "{\"kernel\": \"topk_stream\"}");
+      }
+    }
+  } else {
+    return TARMAC_ERR_MODE;
+  }
+  const int n = (int)strlen(buf);
+  if (n + 1 > len) return TARMAC_ERR_SHAPE;
+  memcpy(out, buf, (size_t)n + 1);
+  return TARMAC_OK;
+}
 
 const char* tarmac_strerror(int status) {
   switch (status) {

@@ -254,14 +254,24 @@ cudaError_t launch_dense_ws(const AttnParams& p, cudaStream_t s);
 // block at a time (dense_tc.cu), the same bits either way — and fp32 with d
 // in {8, 16} and 16-byte rows as three exact bf16 planes; other shapes on
 // the packed-FMA kernel above.
+// 0: persistent warp-specialized, 1: tensor-core per block (bf16), 2:
+// tensor-core per block (fp32 planes), 3: packed FMA
+int dense_plan(const AttnParams& p, int dtype) {
+  if (dtype == TARMAC_BF16 && dense_ws_supported(p)) return 0;
+  if (dtype == TARMAC_BF16 && dense_tc_supported(p)) return 1;
+  if (dtype == TARMAC_F32 && dense_tc_f32_supported(p)) return 2;
+  return 3;
+}
+
 cudaError_t launch_dense(const AttnParams& p, int dtype, cudaStream_t s) {
-  if (dtype == TARMAC_BF16 && dense_ws_supported(p)) return launch_dense_ws(p, s);
-  if (dtype == TARMAC_BF16 && dense_tc_supported(p))
-    return launch_dense_tc(p, s);
-  if (dtype == TARMAC_F32 && dense_tc_f32_supported(p))
-    return launch_dense_tc_f32(p, s);
-  return dtype == TARMAC_BF16 ? launch_dense_dt<__nv_bfloat16>(p, s)
-                              : launch_dense_dt<float>(p, s);
+  switch (dense_plan(p, dtype)) {
+    case 0: return launch_dense_ws(p, s);
+    case 1: return launch_dense_tc(p, s);
+    case 2: return launch_dense_tc_f32(p, s);
+    default:
+      return dtype == TARMAC_BF16 ? launch_dense_dt<__nv_bfloat16>(p, s)
+                                  : launch_dense_dt<float>(p, s);
+  }
 }
 
 }  // namespace tarmac

@@ -83,6 +83,9 @@ SIGNATURES: dict[str, tuple] = {
         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
         c_int, c_int, c_int, c_int, c_float,
         c_void_p, c_void_p, c_void_p, c_void_p]),
+    "tarmac_kernel_plan": (c_int, [
+        c_int, c_int, c_int, c_int, c_int, c_int, c_int, c_void_p,
+        c_char_p, c_int]),
 }
 
 _LOCK = threading.Lock()

@@ -403,3 +403,26 @@ def comm_forward(x: torch.Tensor, w_qkv: torch.Tensor, b_qkv: torch.Tensor,
                   _ptr(w_proj), _ptr(b_proj), B, N, D, m, int(topk),
                   _ptr(out), _stream(x.device))
     return out
+
+
+_PLAN_OPS = {"dense": 0, "topk": 1, "streaming": 2}
+_PLAN_MODES = {"argmax": _lib.SELECT_ARGMAX, "threshold": _lib.SELECT_THRESHOLD,
+               "sort": _lib.SELECT_SORT}
+
+
+def kernel_plan(op: str, B: int, N: int, d: int, dtype: torch.dtype = torch.float32,
+                k: int = 1, mode: str = "argmax") -> dict:
+    """The kernel and tiling a contiguous call of ``op`` ("dense", "topk" or
+    "streaming") with these shapes takes, as the library decides it from the
+    shape: e.g. {"kernel": "topk_ws", "query_tile": 128, "key_tile": 128,
+    "chunk": 8, "chunks_kept": 2}. Host-only (no GPU needed); raises
+    :class:`TarmacError` for arguments the call itself would reject."""
+    import ctypes
+    import json
+    if dtype not in (torch.float32, torch.bfloat16):
+        raise ValueError("dtype must be float32 or bfloat16")
+    dt = _lib.BF16 if dtype == torch.bfloat16 else _lib.F32
+    buf = ctypes.create_string_buffer(256)
+    _lib.call("tarmac_kernel_plan", _PLAN_OPS[op], B, N, d, dt, k,
+              _PLAN_MODES[mode], None, buf, len(buf))
+    return json.loads(buf.value.decode())
