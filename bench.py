@@ -455,8 +455,18 @@ def _comm_c1(ops, dev, stream) -> dict:
         q, kk, v = F.linear(x, w_qkv, b_qkv).chunk(3, dim=-1)
         F.linear(F.gelu(ops.topk_attention(q, kk, v, k)), w_p, b_p)
 
+    # the fused call replayed from a captured graph through the package's
+    # GraphedCall helper (inputs copied into the graph's buffers each call):
+    # what a rollout loop pays per call instead of the Python-level call
+    from tarmac_b200.graphs import GraphedCall
+    gstep = GraphedCall(ops.comm_forward, x, w_qkv, b_qkv, w_p, b_p, k)
+
+    def graphed(s):
+        gstep(x, w_qkv, b_qkv, w_p, b_p, k)
+
     res = {"B": B, "N": N, "in_dim": D, "msg_dim": m, "k": k}
-    for name, fn in (("fused_us", fused), ("layered_us", layered)):
+    for name, fn in (("fused_us", fused), ("layered_us", layered),
+                     ("fused_graphed_call_us", graphed)):
         for s in range(5):
             fn(s)
         t = _time_loop(fn, 200, stream) / 200
