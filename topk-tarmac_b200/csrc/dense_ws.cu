@@ -462,7 +462,11 @@ static bool dws_a16(const void* x) { return reinterpret_cast<uintptr_t>(x) % 16 
 // tiles share each staged K and V tile), d a multiple of 8 from 24 to 64,
 // 16-byte aligned rows. B = 4096, N = 512: d = 64 748 against 891 us,
 // d = 32 571 against 625 us; at d = 16 the per-block kernel is faster (518
-// against 551 us).
+// against 551 us). With fewer episodes per SM it wins only when the batch
+// fills the SMs evenly (d = 64: B = 148 39.2 against 43.4 us, B = 444 94.7
+// against 105.6) and ties or loses otherwise (B = 256 66.5 against 67.6,
+// B = 512 120.3 against 121.3; d = 32, B = 512: 90.6 against 86.7), where the
+// per-block kernel's 128-query blocks balance better.
 bool dense_ws_supported(const AttnParams& p) {
   if (p.B < DWS_MIN_B || p.N < 385 || p.N > DWS_MAX_N || p.d % 8 != 0 || p.d <= 16 ||
       p.d > 64)

@@ -715,17 +715,22 @@ static cudaError_t launch_ws_kc(const AttnParams& p, cudaStream_t s) {
 
 static bool ws_a16(const void* x) { return reinterpret_cast<uintptr_t>(x) % 16 == 0; }
 
-// The persistent kernel serves batches of at least four episodes per SM
-// (fewer leave its pipeline half empty: B = 256 measured 26.7 against
-// 22.7 us) of 385 to 512 agents (four query tiles share each staged K
-// tile). fp32: d a multiple of 8 up to 16, k <= 2 (B = 1024, N = 512:
-// 95.7 against 100.0 us at k = 2; at k = 4 the per-block kernel is faster).
-// bf16: d a multiple of 8 from 24 to 64, k <= 4 where the shared-memory
-// plan fits (B = 4096, N = 512, k = 2: d = 32 313 against 373 us, d = 64
-// 468 against 518 us); at d <= 16 the per-block kernel is as fast.
-constexpr int WS_MIN_B = 4 * 148;
+// The persistent kernel serves episodes of 385 to 512 agents (four query
+// tiles share each staged K tile), measured against the per-block kernel
+// on the same episodes (N = 512, the same bits):
+// * fp32: d a multiple of 8 up to 16, k <= 2, batches of at least two
+//   episodes per SM (k = 2: B = 256 31.0 against 31.1 us, B = 296 31.1
+//   against 34.7, B = 1024 84 against 98.5; k = 1 at B = 256 27.5 against
+//   28.9 for the per-block kernel; at k = 4 the per-block kernel is faster);
+// * bf16: d a multiple of 8 from 24 to 64, k <= 4 where the shared-memory
+//   plan fits, batches of at least one episode per SM (k = 2, B = 148: d = 32
+//   17.2 against 20.8 us, d = 64 24.9 against 26.9; B = 4096: 265 against
+//   373 and 364 against 518); at d <= 16 the per-block kernel is as fast.
+constexpr int WS_MIN_B_F32 = 2 * 148;
+constexpr int WS_MIN_B_BF16 = 148;
 bool topk_ws_supported(const AttnParams& p, int dtype) {
-  if (p.B < WS_MIN_B || p.N < 385 || p.N > WS_MAX_N || p.topk < 1 || p.d % 8 != 0)
+  const int min_b = dtype == TARMAC_BF16 ? WS_MIN_B_BF16 : WS_MIN_B_F32;
+  if (p.B < min_b || p.N < 385 || p.N > WS_MAX_N || p.topk < 1 || p.d % 8 != 0)
     return false;
   const Strides& t = p.st;
   const int64_t al = dtype == TARMAC_BF16 ? 8 : 4;  // elements per 16 bytes
