@@ -1,8 +1,9 @@
 """GPU parity: the persistent warp-specialized top-k kernel (csrc/topk_ws.cu).
 
-It serves batches of at least 592 episodes (four per SM) of 385 to 512
-agents: fp32 with d in {8, 16} and k <= 2, bf16 with d a multiple of 8 from
-24 to 64 and k <= 4. Two checks per case, through the C ABI:
+It serves fp32 batches of at least 296 episodes (two per SM) of 352 to 512
+agents with d in {8, 16} and k <= 2, and bf16 batches of at least 148 (one
+per SM) of 320 to 512 agents with d a multiple of 8 from 24 to 64 and
+k <= 4. Two checks per case, through the C ABI:
 
 * a seeded sample of episodes against the CPU oracle (the bar of every
   top-k test: indices equal on unambiguous rows, outputs within rtol = atol
@@ -48,7 +49,7 @@ def _check(ops, q, k, v, kk, mode="argmax", tie="low"):
     assert torch.equal(i8, idx[:8])
 
 
-@pytest.mark.parametrize("N", [385, 448, 500, 512])
+@pytest.mark.parametrize("N", [352, 384, 385, 448, 500, 512])
 @pytest.mark.parametrize("k", [1, 2])
 def test_fp32_episode_sizes(ops, N, k):
     q, kt, v = qkv(B_WS, N, 16, seed=N + k)
@@ -83,3 +84,17 @@ def test_strided_views_and_streaming_entry(ops):
     a = ops.streaming_topk_attention(q, kt, v, 2)
     b = ops.topk_attention(q, kt, v, 2)
     assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("B,N,d,k", [(148, 320, 32, 2), (150, 333, 64, 1),
+                                     (300, 384, 24, 4), (296, 512, 64, 2)])
+def test_bf16_small_batches_and_three_query_tiles(ops, B, N, d, k):
+    """Batches from one episode per SM and episodes of three query tiles
+    (320-384 agents) take the persistent kernel as well."""
+    q, kt, v = qkv(B, N, d, seed=B + N + d, dtype=torch.bfloat16)
+    _check(ops, q, kt, v, k)
+
+
+def test_fp32_two_episodes_per_sm(ops):
+    q, kt, v = qkv(296, 360, 16, seed=296)
+    _check(ops, q, kt, v, 2)

@@ -715,9 +715,12 @@ static cudaError_t launch_ws_kc(const AttnParams& p, cudaStream_t s) {
 
 static bool ws_a16(const void* x) { return reinterpret_cast<uintptr_t>(x) % 16 == 0; }
 
-// The persistent kernel serves episodes of 385 to 512 agents (four query
-// tiles share each staged K tile), measured against the per-block kernel
-// on the same episodes (N = 512, the same bits):
+// The persistent kernel serves episodes of up to 512 agents whose three or
+// four query tiles share each staged K tile: from 320 agents for bf16 and
+// 352 for fp32 (N = 384, B = 4096, k = 2: fp32 210 against 234 us, bf16 d = 32
+// 187 against 242; at N = 272 the per-block kernel is ahead, at N = 320 to
+// 352 they meet). Measured against the per-block kernel on the same
+// episodes (N = 512, the same bits):
 // * fp32: d a multiple of 8 up to 16, k <= 2, batches of at least two
 //   episodes per SM (k = 2: B = 256 31.0 against 31.1 us, B = 296 31.1
 //   against 34.7, B = 1024 84 against 98.5; k = 1 at B = 256 27.5 against
@@ -730,7 +733,8 @@ constexpr int WS_MIN_B_F32 = 2 * 148;
 constexpr int WS_MIN_B_BF16 = 148;
 bool topk_ws_supported(const AttnParams& p, int dtype) {
   const int min_b = dtype == TARMAC_BF16 ? WS_MIN_B_BF16 : WS_MIN_B_F32;
-  if (p.B < min_b || p.N < 385 || p.N > WS_MAX_N || p.topk < 1 || p.d % 8 != 0)
+  const int min_n = dtype == TARMAC_BF16 ? 320 : 352;
+  if (p.B < min_b || p.N < min_n || p.N > WS_MAX_N || p.topk < 1 || p.d % 8 != 0)
     return false;
   const Strides& t = p.st;
   const int64_t al = dtype == TARMAC_BF16 ? 8 : 4;  // elements per 16 bytes
