@@ -1,6 +1,6 @@
 """GPU parity: the persistent warp-specialized dense kernel (csrc/dense_ws.cu).
 
-It serves bf16 batches of at least 592 episodes (four per SM) of 385 to 512
+It serves bf16 batches of at least 592 episodes (four per SM) of 320 to 512
 agents with d a multiple of 8 up to 64. Two checks per case, through the
 C ABI:
 
@@ -44,7 +44,7 @@ def _check(ops, q, k, v):
     assert torch.equal(head, out[:8])
 
 
-@pytest.mark.parametrize("N", [385, 448, 512])
+@pytest.mark.parametrize("N", [320, 384, 385, 448, 512])
 @pytest.mark.parametrize("d", [16, 64])
 def test_episode_sizes_and_widths(ops, N, d):
     q, kt, v = qkv(B_WS, N, d, seed=N * 3 + d, dtype=torch.bfloat16)

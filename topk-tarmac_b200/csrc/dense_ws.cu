@@ -1,6 +1,6 @@
 // dense_ws.cu — dense masked-diagonal attention on the tensor cores for bf16
 // inputs, warp-specialized and persistent: one block per SM loops over whole
-// episodes of 385 to 512 agents.
+// episodes of 320 to 512 agents.
 //
 // Same function and the same arithmetic as dense_tc.cu (reference:
 // src/kernels/fused_dense_attention.py:38-99): per 64-key tile, S = Q K^T
@@ -458,9 +458,10 @@ static cudaError_t launch_dws_t(const AttnParams& p, cudaStream_t s) {
 
 static bool dws_a16(const void* x) { return reinterpret_cast<uintptr_t>(x) % 16 == 0; }
 
-// bf16, batches of at least four episodes per SM, 385-512 agents (four query
-// tiles share each staged K and V tile), d a multiple of 8 from 24 to 64,
-// 16-byte aligned rows. B = 4096, N = 512: d = 64 748 against 891 us,
+// bf16, batches of at least four episodes per SM, 320-512 agents (three or
+// four query tiles share each staged K and V tile; N = 320, B = 4096: d = 64
+// 410 against 473 us, d = 32 297 against 327; at N = 256 the two are even),
+// d a multiple of 8 from 24 to 64, 16-byte aligned rows. B = 4096, N = 512: d = 64 748 against 891 us,
 // d = 32 571 against 625 us; at d = 16 the per-block kernel is faster (518
 // against 551 us). With fewer episodes per SM it wins only when the batch
 // fills the SMs evenly (d = 64: B = 148 39.2 against 43.4 us, B = 444 94.7
@@ -468,7 +469,7 @@ static bool dws_a16(const void* x) { return reinterpret_cast<uintptr_t>(x) % 16 
 // B = 512 120.3 against 121.3; d = 32, B = 512: 90.6 against 86.7), where the
 // per-block kernel's 128-query blocks balance better.
 bool dense_ws_supported(const AttnParams& p) {
-  if (p.B < DWS_MIN_B || p.N < 385 || p.N > DWS_MAX_N || p.d % 8 != 0 || p.d <= 16 ||
+  if (p.B < DWS_MIN_B || p.N < 320 || p.N > DWS_MAX_N || p.d % 8 != 0 || p.d <= 16 ||
       p.d > 64)
     return false;
   const Strides& t = p.st;
