@@ -45,7 +45,7 @@ def _check(ops, q, k, v):
 
 
 @pytest.mark.parametrize("N", [320, 384, 385, 448, 512])
-@pytest.mark.parametrize("d", [16, 64])
+@pytest.mark.parametrize("d", [16, 32, 64])
 def test_episode_sizes_and_widths(ops, N, d):
     q, kt, v = qkv(B_WS, N, d, seed=N * 3 + d, dtype=torch.bfloat16)
     _check(ops, q, kt, v)

@@ -13,13 +13,14 @@
 // Roles of the 20 warps:
 // * warps 0..15 — four consumer groups; group g owns query tile g (rows
 //   [128 g, 128 g + 128)) and TMEM columns [128 g, 128 g + 128): S in the
-//   first 64, the output accumulator O in the next d. Per tile it reads S,
-//   releases it at once (the next tile's Q K^T runs under the softmax),
-//   computes the weights, waits for the previous P V, rescales O when its
-//   reference moved, writes P to its shared-memory tile and announces it.
+//   first 64, the output accumulator O in the next d and, for d <= 32, P
+//   (bf16 pairs) in the last 32. Per tile it reads S, releases it at once
+//   (the next tile's Q K^T runs under the softmax), computes the weights,
+//   waits for the previous P V, rescales O when its reference moved, writes
+//   P (to TMEM for d <= 32, else to its shared-memory tile) and announces it.
 // * warps 16, 17 — K/V producers: each 64-key K tile (K-major) and V tile
 //   (MN-major, its rows are the contraction dimension) is staged once per
-//   episode into a ring read by all four groups; they also prefetch the
+//   episode into a ring (2 to 8 slots) read by all four groups; they also prefetch the
 //   next episode's K and V rows into L2.
 // * warp 18 — Q producer (two Q buffers: the next episode's Q is staged
 //   while the current one runs).
@@ -49,8 +50,10 @@ constexpr int DWS_SMEM_LIMIT = 227 * 1024;  // the per-block maximum (232,448 by
 constexpr float DWS_LOG2E = 1.4426950408889634f;
 constexpr float DWS_RESCALE_LOG2 = 8.0f;
 
+constexpr int DWS_MAX_NS = 8;         // K/V ring slots (max)
+
 struct DwsShared {
-  uint64_t kvfull[4], kvempty[4];
+  uint64_t kvfull[DWS_MAX_NS], kvempty[DWS_MAX_NS];
   uint64_t qfull[2][DWS_NQ], qempty[2][DWS_NQ];
   uint64_t sfull[DWS_NQ], sempty[DWS_NQ];
   uint64_t pfull[DWS_NQ], pvdone[DWS_NQ];
@@ -62,14 +65,19 @@ template <int DP>
 struct DwsPlan {
   static constexpr int QTILE = 128 * DP * 2;
   static constexpr int KVTILE = DWS_KEYS * DP * 2;       // one K or V tile
+  // d <= 32: P in tensor memory beside S and O (64 + 32 + 32 columns), the
+  // A operand of P V; that takes P's stores and half of P V's operand reads
+  // off the shared-memory pipe (B = 4096, N = 512, d = 32: 547 against 571 us)
+  static constexpr bool PT = DP <= 32;
   static constexpr int PTILE = 128 * DWS_KEYS * 2;       // one group's P
-  static constexpr int PBYTES = DWS_NQ * PTILE;
-  // two Q buffers first, then as many K/V ring slots (2..4) as fit
+  static constexpr int PBYTES = PT ? 0 : DWS_NQ * PTILE;
+  // two Q buffers first, then as many K/V ring slots (2..8) as fit
   static constexpr int NQB = (2 * DWS_NQ * QTILE + 2 * 2 * KVTILE + PBYTES <=
                               DWS_SMEM_LIMIT) ? 2 : 1;
   static constexpr int QBYTES = NQB * DWS_NQ * QTILE;
   static constexpr int FREE = DWS_SMEM_LIMIT - QBYTES - PBYTES;
-  static constexpr int NS = FREE >= 4 * 2 * KVTILE ? 4 : (FREE >= 3 * 2 * KVTILE ? 3 : 2);
+  static constexpr int NS0 = FREE / (2 * KVTILE);
+  static constexpr int NS = NS0 > DWS_MAX_NS ? DWS_MAX_NS : NS0;
   static constexpr int KVBYTES = NS * 2 * KVTILE;
   static constexpr int TOTAL = QBYTES + KVBYTES + PBYTES;
 };
@@ -91,6 +99,24 @@ __device__ __forceinline__ void copy_tile_mn_bf16(uint32_t base,
     cp16(base + (uint32_t)(((r >> 3) + c * (R >> 3)) * 128 + (r & 7) * 16),
          ok ? src + (int64_t)r * rs + c * 8 : src, ok);
   }
+}
+// 32 consecutive 32-bit columns into this thread's TMEM lane (warp-collective);
+// complete when the call returns
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n"
+               "tcgen05.wait::st.sync.aligned;" ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+               : "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem], issued by one thread (A K-major in TMEM:
+// lane m, column k / 2, the lower k in the low half)
+__device__ __forceinline__ void mma_bf16_ts(uint32_t tmem_d, uint32_t tmem_a,
+                                            uint64_t bdesc, uint32_t idesc,
+                                            bool accumulate) {
+  asm volatile(
+      "{\n.reg .pred p;\nsetp.ne.b32 p, %4, 0;\n"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate));
 }
 }  // namespace ws
 
@@ -228,7 +254,7 @@ __global__ void __launch_bounds__(DWS_THREADS, 1) dense_ws_kernel(AttnParams p) 
         int ns[DWS_NQ] = {0, 0, 0, 0}, np[DWS_NQ] = {0, 0, 0, 0};
         // per ring slot (8 bits each): groups whose P V of the slot's tile
         // has been issued
-        uint32_t pvcnt = 0;
+        uint64_t pvcnt = 0;
         int finished = 0;
         uint32_t idle = 0;
         while (finished < nqt) {
@@ -264,15 +290,22 @@ __global__ void __launch_bounds__(DWS_THREADS, 1) dense_ws_kernel(AttnParams p) 
               const uint32_t kj = kc + (uint32_t)np[g];
               const int s = kj % NS;
               const uint64_t dv = dv0 + (uint64_t)((s * 2 * KVTILE) >> 4);
-              const uint64_t dp = dp0 + (uint64_t)((g * PTILE) >> 4);
+              if constexpr (Plan::PT) {
 #pragma unroll
-              for (int ks = 0; ks < DWS_KEYS / 16; ++ks)
-                tc::mma_bf16(tmem + g * 128 + DWS_KEYS, dp + (uint64_t)(ks * 16),
-                             dv + (uint64_t)(ks * 16), idesc_o, np[g] > 0 || ks > 0);
+                for (int ks = 0; ks < DWS_KEYS / 16; ++ks)
+                  ws::mma_bf16_ts(tmem + g * 128 + DWS_KEYS, tmem + g * 128 + DWS_KEYS + 32 + ks * 8,
+                                  dv + (uint64_t)(ks * 16), idesc_o, np[g] > 0 || ks > 0);
+              } else {
+                const uint64_t dp = dp0 + (uint64_t)((g * PTILE) >> 4);
+#pragma unroll
+                for (int ks = 0; ks < DWS_KEYS / 16; ++ks)
+                  tc::mma_bf16(tmem + g * 128 + DWS_KEYS, dp + (uint64_t)(ks * 16),
+                               dv + (uint64_t)(ks * 16), idesc_o, np[g] > 0 || ks > 0);
+              }
               tc::mma_commit(&sh.pvdone[g]);
-              pvcnt += 1u << (8 * s);
-              if (((pvcnt >> (8 * s)) & 0xffu) == (uint32_t)nqt) {
-                pvcnt &= ~(0xffu << (8 * s));
+              pvcnt += 1ull << (8 * s);
+              if (((pvcnt >> (8 * s)) & 0xffu) == (uint64_t)nqt) {
+                pvcnt &= ~(0xffull << (8 * s));
                 tc::mma_commit(&sh.kvempty[s]);
               }
               if (++np[g] == nt) ++finished;
@@ -385,16 +418,23 @@ __global__ void __launch_bounds__(DWS_THREADS, 1) dense_ws_kernel(AttnParams p) 
             tc::tmem_st8(t_o + lane_off + c, o8);
           }
         }
+        if constexpr (Plan::PT) {
+          uint32_t pw[DWS_KEYS / 2];
 #pragma unroll
-        for (int c = 0; c < PCH; ++c) {
-          uint4 w;
-          w.x = tc::pack_bf16x2(s[8 * c], s[8 * c + 1]);
-          w.y = tc::pack_bf16x2(s[8 * c + 2], s[8 * c + 3]);
-          w.z = tc::pack_bf16x2(s[8 * c + 4], s[8 * c + 5]);
-          w.w = tc::pack_bf16x2(s[8 * c + 6], s[8 * c + 7]);
-          *reinterpret_cast<uint4*>(prow + c * 128) = w;
+          for (int t = 0; t < DWS_KEYS / 2; ++t) pw[t] = tc::pack_bf16x2(s[2 * t], s[2 * t + 1]);
+          ws::tmem_st32(t_o + 32 + lane_off, pw);
+        } else {
+#pragma unroll
+          for (int c = 0; c < PCH; ++c) {
+            uint4 w;
+            w.x = tc::pack_bf16x2(s[8 * c], s[8 * c + 1]);
+            w.y = tc::pack_bf16x2(s[8 * c + 2], s[8 * c + 3]);
+            w.z = tc::pack_bf16x2(s[8 * c + 4], s[8 * c + 5]);
+            w.w = tc::pack_bf16x2(s[8 * c + 6], s[8 * c + 7]);
+            *reinterpret_cast<uint4*>(prow + c * 128) = w;
+          }
+          tc::fence_async_smem();
         }
-        tc::fence_async_smem();
         tc::fence_before_sync();
         __syncwarp();
         if (lane == 0) ws::arrive(&sh.pfull[g]);
