@@ -487,6 +487,131 @@ def _comm_c1(ops, dev, stream) -> dict:
     return res
 
 
+# the unmodified reference tree (git-ignored; it travels with the repository
+# snapshot): its eager GPU code is the comparison for the gradient and
+# selector rows below, where the reference has no kernel of its own
+REF_TREE = REPO / "baseline" / "_ref" / "TopK-TarMAC"
+
+
+def _ref_module(rel: str, name: str):
+    """One module of the reference tree loaded by file path (its ``src``
+    package name is taken by the drop-in), or None when the tree is absent."""
+    import importlib.util
+    path = REF_TREE / rel
+    if not path.is_file():
+        return None
+    saved = list(sys.path)
+    try:
+        spec = importlib.util.spec_from_file_location(name, path)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        return mod
+    finally:
+        sys.path[:] = saved
+
+
+def _next_rows(ops, dev, stream, fp32_tf) -> dict:
+    """The rows after the attention core, measured (informational, warm L2):
+
+    * gradients (training): forward + backward through the package's
+      autograd functions against the reference's eager forward under torch
+      autograd on the same GPU (reference_topk_attention,
+      src/kernels/fused_topk_attention.py:390-402; dense_unfused,
+      scripts/bench_attention_core.py:74-75), at C2 (B=1024, N=512, d=16,
+      k=2, fp32) and at the MPE training shape (B=256, N=6); plus the
+      gradient kernels alone (device time, CUDA graph replay) against their
+      roofs: HBM bytes for the fixed-peer kernel ((2 + 3k) d s read and
+      3 d 4 written per row), FFMA flops for the dense pair (9 N^2 d per
+      episode) against this run's fp32 cuBLAS figure;
+    * selectors: exact kNN, grid kNN and random k peers at the C4 shape
+      (N=512, k=2, B=1024 and 4096) against the reference's eager selectors
+      on the same GPU (select_radius_knn and select_grid_knn,
+      src/kernels/prescore_selection.py:35-48, 107-165; the random-k draw of
+      src/agents/mappo.py:251-254, restated here: uniform noise, self
+      excluded, the k smallest)."""
+    import torch
+    from tarmac_b200 import autograd as ag
+
+    ref_fta = _ref_module("src/kernels/fused_topk_attention.py", "_ref_fta")
+    ref_bac = _ref_module("scripts/bench_attention_core.py", "_ref_bac")
+    ref_ps = _ref_module("src/kernels/prescore_selection.py", "_ref_ps")
+    out = {"reference_tree": "present" if ref_fta is not None else
+           "absent (the reference columns are null)"}
+
+    def timed(fn, reps):
+        for s in range(3):
+            fn(s)
+        torch.cuda.synchronize(dev)
+        return round(1e3 * _time_loop(fn, reps, stream) / reps, 2)
+
+    grads = []
+    for B_, N_, reps in ((1024, 512, 20), (256, 6, 200)):
+        d_, k_ = 16, 2
+        g = torch.Generator().manual_seed(1234 + 7 * N_ + d_)
+        q, k, v, go = (torch.randn(B_, N_, d_, generator=g).to(dev)
+                       for _ in range(4))
+        qg, kg, vg = (t.clone().requires_grad_(True) for t in (q, k, v))
+        eye = torch.eye(N_, device=dev, dtype=torch.bool).unsqueeze(0)
+
+        def fb(f):
+            return lambda s: torch.autograd.grad(f(), (qg, kg, vg), go)
+
+        row = {"B": B_, "N": N_, "d": d_, "k": k_, "dtype": "f32"}
+        row["topk_fwd_bwd_us"] = timed(fb(lambda: ag.topk_attention(qg, kg, vg, k_)), reps)
+        row["dense_fwd_bwd_us"] = timed(fb(lambda: ag.dense_attention(qg, kg, vg)), reps)
+        if ref_fta is not None:
+            row["ref_eager_topk_fwd_bwd_us"] = timed(
+                fb(lambda: ref_fta.reference_topk_attention(qg, kg, vg, k_)), reps)
+        if ref_bac is not None:
+            row["ref_eager_dense_fwd_bwd_us"] = timed(
+                fb(lambda: ref_bac.dense_unfused(qg, kg, vg, eye, k_)), reps)
+        # the gradient kernels alone
+        _, idx = ops.topk_attention(q, k, v, k_, return_indices=True)
+        o_d = ops.dense_attention(q, k, v)
+        t_g, _ = _graph_us(lambda s: ops.gather_attention_backward(q, k, v, go, idx),
+                           dev, stream)
+        t_d, _ = _graph_us(lambda s: ops.dense_attention_backward(q, k, v, o_d, go),
+                           dev, stream)
+        row["topk_bwd_kernel_dev_us"], row["dense_bwd_kernels_dev_us"] = t_g, t_d
+        rows_ = B_ * N_
+        gbytes = rows_ * ((2 + 3 * k_) * d_ * 4 + 3 * d_ * 4)
+        if t_g:
+            row["topk_bwd_hbm_frac"] = round(gbytes / (t_g * 1e-6) / 1e9
+                                             / _peaks()["hbm_gbs"], 3)
+        if t_d and fp32_tf:
+            tf = 9 * B_ * N_ * N_ * d_ / (t_d * 1e-6) / 1e12
+            row["dense_bwd_tflops"] = round(tf, 2)
+            row["dense_bwd_frac_of_fp32_simt_gemm"] = round(tf / fp32_tf, 3)
+        grads.append(row)
+        del q, k, v, go, qg, kg, vg, idx, o_d
+    out["gradients"] = grads
+
+    sels = []
+    for B_ in (1024, 4096):
+        N_, k_ = 512, 2
+        g = torch.Generator().manual_seed(4242 + N_)
+        pos = torch.rand(B_, N_, 2, generator=g).to(dev)
+        eye = torch.eye(N_, device=dev, dtype=torch.bool).unsqueeze(0)
+        row = {"B": B_, "N": N_, "k": k_}
+        row["knn_us"] = timed(lambda s: ops.knn_select(pos, k_), 30)
+        row["grid_knn_us"] = timed(lambda s: ops.grid_knn_select(pos, k_), 30)
+        row["random_k_us"] = timed(lambda s: ops.random_select(B_, N_, k_, dev), 30)
+        if ref_ps is not None:
+            row["ref_eager_knn_us"] = timed(lambda s: ref_ps.select_radius_knn(pos, k_), 10)
+            row["ref_eager_grid_knn_us"] = timed(
+                lambda s: ref_ps.select_grid_knn(pos, k_), 10)
+
+        def ref_random(s):
+            noise = torch.rand(B_, N_, N_, device=dev).masked_fill(eye, float("inf"))
+            return noise.topk(k_, dim=-1, largest=False, sorted=False).indices
+
+        row["ref_eager_random_k_us"] = timed(ref_random, 10)
+        sels.append(row)
+        del pos
+    out["selectors"] = sels
+    return out
+
+
 def _fp32_peak(dev) -> float:
     """Measured fp32 (TF32 off) cuBLAS GEMM TFLOP/s: the FFMA roof the fp32
     top-k kernel is bound by (not a tensor-core figure)."""
@@ -683,6 +808,8 @@ def run_ours(args) -> int:
     comm_c1 = _comm_c1(ops, dev, stream) if rank == 0 and not args.no_sweep else {}
 
     fp32_tf = _fp32_peak(dev) if rank == 0 else None
+    next_rows = (_next_rows(ops, dev, stream, fp32_tf)
+                 if rank == 0 and not multi and not args.no_sweep else {})
     if multi:
         shard.barrier(dev)
     if rank != 0:
@@ -764,6 +891,7 @@ def run_ours(args) -> int:
         "sweep_c3_stream_us": sweep_c3,
         "sweep_c4_zorder": sweep_c4,
         "comm_module_c1": comm_c1,
+        "next_rows": next_rows,
     }
     if world == 1 and not args.no_cpu:
         line["cpu_baseline"] = cpu_baseline(args.cpu_episodes, args.cpu_seconds)
