@@ -165,6 +165,15 @@ __global__ void __launch_bounds__(128) gather_bwd_kernel(BwdParams p) {
 // ---------------------------------------------------------------------------
 
 constexpr int BWD_TILE = 32;  // streamed rows per shared-memory tile
+constexpr float BWD_LOG2E = 1.4426950408889634f;
+constexpr float BWD_RESCALE_LOG2 = 8.0f;  // see the log-sum-exp pass below
+
+// 2^x by the hardware approximation (relative error about 2^-22; 2^-inf = 0)
+__device__ __forceinline__ float bwd_ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 template <int DP>
 __host__ __device__ constexpr int bwd_cpl() { return DP < 32 ? DP : 32; }
@@ -209,27 +218,29 @@ __global__ void __launch_bounds__(128) dense_bwd_dq_kernel(BwdParams p) {
                               (int64_t)ii * p.on, c0, d, vec);
   const float D = group_sum<LPR>(dotc<CPL>(gr, orow));
   const float sc = p.scale;
+  const float c2 = sc * BWD_LOG2E;  // scores in base-2 exponent units
 
-  // pass 1: row log-sum-exp over the keys j != i
-  float mx = -INFINITY, sum = 0.f;
+  // pass 1: row log-sum-exp (base 2) over the keys j != i. The reference
+  // point moves only when a score exceeds it by more than 2^8, so each key
+  // costs one exponential and the terms stay below 2^8 (no overflow).
+  float mref = -INFINITY, sum = 0.f;
   for (int t0 = 0; t0 < N; t0 += BWD_TILE) {
     __syncthreads();
     stage_f32<DP, T>(sk, K, p.kn, t0, N, d);
     __syncthreads();
     const int nt = min(BWD_TILE, N - t0);
     for (int jj = 0; jj < nt; ++jj) {
-      const float s = group_sum<LPR>(dotc<CPL>(qr, sk + jj * DP + c0)) * sc;
+      const float s = group_sum<LPR>(dotc<CPL>(qr, sk + jj * DP + c0)) * c2;
       if (t0 + jj != i) {  // no collective inside: lanes may diverge here
-        if (s > mx) {
-          sum = sum * expf(mx - s) + 1.f;
-          mx = s;
-        } else {
-          sum += expf(s - mx);
+        if (s > mref + BWD_RESCALE_LOG2) {
+          sum *= bwd_ex2(mref - s);
+          mref = s;
         }
+        sum += bwd_ex2(s - mref);
       }
     }
   }
-  const float lse = mx + logf(sum);
+  const float lse = mref + log2f(sum);
   // pass 2: dq
   float acc[CPL];
 #pragma unroll
@@ -242,9 +253,9 @@ __global__ void __launch_bounds__(128) dense_bwd_dq_kernel(BwdParams p) {
     const int nt = min(BWD_TILE, N - t0);
     for (int jj = 0; jj < nt; ++jj) {
       const float* kr = sk + jj * DP + c0;
-      const float s = group_sum<LPR>(dotc<CPL>(qr, kr)) * sc;
+      const float s = group_sum<LPR>(dotc<CPL>(qr, kr)) * c2;
       const float dp = group_sum<LPR>(dotc<CPL>(gr, sv + jj * DP + c0));
-      const float pw = (t0 + jj == i) ? 0.f : expf(s - lse);
+      const float pw = (t0 + jj == i) ? 0.f : bwd_ex2(s - lse);
       const float ds = pw * (dp - D);
 #pragma unroll
       for (int c = 0; c < CPL; ++c) acc[c] = fmaf(ds, kr[c], acc[c]);
@@ -294,6 +305,7 @@ __global__ void __launch_bounds__(128) dense_bwd_dkdv_kernel(BwdParams p) {
     dv[c] = 0.f;
   }
   const float sc = p.scale;
+  const float c2 = sc * BWD_LOG2E;
   for (int t0 = 0; t0 < N; t0 += BWD_TILE) {
     __syncthreads();
     stage_f32<DP, T>(sq, Q, p.qn, t0, N, d);
@@ -308,9 +320,9 @@ __global__ void __launch_bounds__(128) dense_bwd_dkdv_kernel(BwdParams p) {
     for (int q = 0; q < nt; ++q) {
       const float* qrow = sq + q * DP + c0;
       const float* grow = sg + q * DP + c0;
-      const float s = group_sum<LPR>(dotc<CPL>(kr, qrow)) * sc;
+      const float s = group_sum<LPR>(dotc<CPL>(kr, qrow)) * c2;
       const float dp = group_sum<LPR>(dotc<CPL>(vr, grow));
-      const float pw = (t0 + q == j) ? 0.f : expf(s - slse[q]);
+      const float pw = (t0 + q == j) ? 0.f : bwd_ex2(s - slse[q]);
       const float ds = pw * (dp - sD[q]);
 #pragma unroll
       for (int c = 0; c < CPL; ++c) {

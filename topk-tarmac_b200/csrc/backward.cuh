@@ -18,7 +18,7 @@ struct BwdParams {
   float* dq;
   float* dk;
   float* dv;
-  float* work;       // dense: [2][B][N] row log-sum-exp, then D
+  float* work;       // dense: [2][B][N] row log-sum-exp (base 2), then D
   const void* idx;   // gather: [B, N, kk]
   int idx_i64;
   int kk;
