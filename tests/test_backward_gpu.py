@@ -163,3 +163,33 @@ def test_strided_views_receive_gradients(tb):
     want = oracle.gather_attention_grad(host(q), host(k), host(v),
                                         idx.long().cpu().numpy(), host(g))
     close(x.grad, np.concatenate(want, axis=-1))
+
+
+def test_gather_backward_gradients_off_the_16_byte_grid(tb):
+    """Through the C ABI with dk and dv starting 4 bytes past a 16-byte
+    boundary: the kernel falls back from four-column vector reductions to
+    scalar ones and returns the same gradients."""
+    ops, _ = tb
+    from tarmac_b200 import _lib
+    B, N, d, kk = 3, 64, 16, 4
+    q, k, v = qkv(B, N, d, seed=77)
+    gen = torch.Generator().manual_seed(78)
+    g = torch.randn(B, N, d, generator=gen).cuda()
+    idx = torch.randint(0, N, (B, N, kk), generator=gen).cuda()
+    want = ops.gather_attention_backward(q, k, v, g, idx)
+    dq = torch.empty(B, N, d, device="cuda")
+    dk_buf = torch.full((B * N * d + 4,), float("nan"), device="cuda")
+    dv_buf = torch.full((B * N * d + 4,), float("nan"), device="cuda")
+    dk, dv = dk_buf[1:1 + B * N * d], dv_buf[1:1 + B * N * d]
+    assert dk.data_ptr() % 16 == 4
+    strides = ops._strides_n(q, k, v, g)
+    with ops._on(q.device):
+        _lib.call("tarmac_gather_attention_backward", q.data_ptr(), k.data_ptr(),
+                  v.data_ptr(), g.data_ptr(), strides, idx.data_ptr(), 1, kk, B, N,
+                  d, _lib.F32, 1.0 / d ** 0.5, dq.data_ptr(), dk.data_ptr(),
+                  dv.data_ptr(), ops._stream(q.device))
+    torch.cuda.synchronize()
+    close(dq, host(want[0]))
+    close(dk.view(B, N, d), host(want[1]))
+    close(dv.view(B, N, d), host(want[2]))
+    assert torch.isnan(dk_buf[0]) and torch.isnan(dk_buf[-3:]).all()

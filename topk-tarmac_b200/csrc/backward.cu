@@ -131,6 +131,9 @@ __global__ void __launch_bounds__(128) gather_bwd_kernel(BwdParams p) {
   const bool row_ok = live && !bad;
   float* dK = p.dk + (int64_t)b * N * d;
   float* dV = p.dv + (int64_t)b * N * d;
+  // vector reductions need every row of dk and dv on a 16-byte boundary
+  const bool vred = d % 4 == 0 &&
+                    ((reinterpret_cast<uintptr_t>(p.dk) | reinterpret_cast<uintptr_t>(p.dv)) & 15u) == 0;
   for (int m = 0; m < p.kk; ++m) {
     const int j = peer(m);
     float k4[4], v4[4];
@@ -144,11 +147,22 @@ __global__ void __launch_bounds__(128) gather_bwd_kernel(BwdParams p) {
     if (row_ok) {
       float* dkr = dK + (int64_t)j * d + c0;
       float* dvr = dV + (int64_t)j * d + c0;
+      if (vred) {
+        // four columns per vector reduction (rows start on 16 bytes)
+        if (c0 < d) {
+          atomicAdd(reinterpret_cast<float4*>(dkr),
+                    make_float4(sc * ds * q4[0], sc * ds * q4[1], sc * ds * q4[2],
+                                sc * ds * q4[3]));
+          atomicAdd(reinterpret_cast<float4*>(dvr),
+                    make_float4(w * g4[0], w * g4[1], w * g4[2], w * g4[3]));
+        }
+      } else {
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        if (c0 + c < d) {
-          atomicAdd(dkr + c, sc * ds * q4[c]);
-          atomicAdd(dvr + c, w * g4[c]);
+        for (int c = 0; c < 4; ++c) {
+          if (c0 + c < d) {
+            atomicAdd(dkr + c, sc * ds * q4[c]);
+            atomicAdd(dvr + c, w * g4[c]);
+          }
         }
       }
     }
