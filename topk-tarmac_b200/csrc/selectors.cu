@@ -53,6 +53,29 @@ __device__ __forceinline__ void knn_row(const float2* sp, int N, int i,
   }
 }
 
+// the same for agents i and i2 in one pass over the positions (each position
+// read from shared memory once for both rows); i2 >= N computes nothing
+// that is kept
+template <int KM>
+__device__ __forceinline__ void knn_row2(const float2* sp, int N, int i, int i2,
+                                         float (&bs)[KM], int (&bi)[KM],
+                                         float (&bs2)[KM], int (&bi2)[KM]) {
+#pragma unroll
+  for (int m = 0; m < KM; ++m) {
+    bs[m] = -INFINITY;
+    bi[m] = -1;
+    bs2[m] = -INFINITY;
+    bi2[m] = -1;
+  }
+  const float2 pi = sp[i], pi2 = sp[i2 < N ? i2 : i];
+  for (int j = 0; j < N; ++j) {
+    const float2 pj = sp[j];
+    const float nd = -dist2(pi, pj), nd2 = -dist2(pi2, pj);
+    if (j != i && nd > bs[KM - 1]) buf_insert<KM, false>(bs, bi, nd, j);
+    if (j != i2 && nd2 > bs2[KM - 1]) buf_insert<KM, false>(bs2, bi2, nd2, j);
+  }
+}
+
 template <int KM>
 __global__ void __launch_bounds__(SEL_THREADS) knn_select_kernel(
     const float* __restrict__ pos, int N, int k, int64_t* __restrict__ out) {
@@ -61,14 +84,22 @@ __global__ void __launch_bounds__(SEL_THREADS) knn_select_kernel(
   const float2* pe = reinterpret_cast<const float2*>(pos) + (int64_t)b * N;
   for (int i = threadIdx.x; i < N; i += blockDim.x) sel_sp[i] = pe[i];
   __syncthreads();
-  for (int i = threadIdx.x; i < N; i += blockDim.x) {
-    float bs[KM];
-    int bi[KM];
-    knn_row<KM>(sel_sp, N, i, bs, bi);
+  // two agents a thread per pass (i and i + blockDim.x)
+  for (int i = threadIdx.x; i < N; i += 2 * blockDim.x) {
+    const int i2 = i + blockDim.x;
+    float bs[KM], bs2[KM];
+    int bi[KM], bi2[KM];
+    knn_row2<KM>(sel_sp, N, i, i2, bs, bi, bs2, bi2);
     int64_t* o = out + ((int64_t)b * N + i) * k;
 #pragma unroll
     for (int m = 0; m < KM; ++m)
       if (m < k) o[m] = bi[m];
+    if (i2 < N) {
+      int64_t* o2 = out + ((int64_t)b * N + i2) * k;
+#pragma unroll
+      for (int m = 0; m < KM; ++m)
+        if (m < k) o2[m] = bi2[m];
+    }
   }
 }
 
