@@ -68,11 +68,15 @@ __device__ __forceinline__ void knn_row2(const float2* sp, int N, int i, int i2,
     bi2[m] = -1;
   }
   const float2 pi = sp[i], pi2 = sp[i2 < N ? i2 : i];
+#pragma unroll 4
   for (int j = 0; j < N; ++j) {
     const float2 pj = sp[j];
     const float nd = -dist2(pi, pj), nd2 = -dist2(pi2, pj);
-    if (j != i && nd > bs[KM - 1]) buf_insert<KM, false>(bs, bi, nd, j);
-    if (j != i2 && nd2 > bs2[KM - 1]) buf_insert<KM, false>(bs2, bi2, nd2, j);
+    // one test for both rows on the common path (neither enters)
+    if (nd > bs[KM - 1] || nd2 > bs2[KM - 1]) {
+      if (j != i && nd > bs[KM - 1]) buf_insert<KM, false>(bs, bi, nd, j);
+      if (j != i2 && nd2 > bs2[KM - 1]) buf_insert<KM, false>(bs2, bi2, nd2, j);
+    }
   }
 }
 
