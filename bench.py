@@ -559,6 +559,18 @@ def _next_rows(ops, dev, stream, fp32_tf) -> dict:
         row = {"B": B_, "N": N_, "d": d_, "k": k_, "dtype": "f32"}
         row["topk_fwd_bwd_us"] = timed(fb(lambda: ag.topk_attention(qg, kg, vg, k_)), reps)
         row["dense_fwd_bwd_us"] = timed(fb(lambda: ag.dense_attention(qg, kg, vg)), reps)
+        if N_ <= 64:
+            # the same step replayed from CUDA graphs (forward and backward
+            # captured by torch.cuda.make_graphed_callables): what a training
+            # loop at this shape pays without the per-call host work
+            try:
+                gfn = torch.cuda.make_graphed_callables(
+                    lambda a, b_, c: ag.topk_attention(a, b_, c, k_), (qg, kg, vg))
+                row["topk_fwd_bwd_graphed_us"] = timed(
+                    lambda s: torch.autograd.grad(gfn(qg, kg, vg), (qg, kg, vg), go), reps)
+            except RuntimeError as exc:  # capture refused: report why
+                row["topk_fwd_bwd_graphed_us"] = None
+                row["graphed_note"] = str(exc).splitlines()[0][:120]
         if ref_fta is not None:
             row["ref_eager_topk_fwd_bwd_us"] = timed(
                 fb(lambda: ref_fta.reference_topk_attention(qg, kg, vg, k_)), reps)

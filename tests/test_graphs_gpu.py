@@ -56,3 +56,35 @@ def test_mismatched_arguments_raise():
     step2 = GraphedCall(ops.topk_attention, q, k, v, 2)
     with pytest.raises(ValueError):
         step2(q, k, v, 3)                     # other k
+
+
+@pytest.mark.parametrize("op", ["topk", "dense"])
+def test_training_step_graphed_with_torch(op):
+    """The autograd functions are capturable: torch.cuda.make_graphed_callables
+    records forward and backward (kernels, workspace and gradient buffers
+    allocated through torch on the capturing stream) and the replays give the
+    gradients of eager calls. The dense gradients are deterministic (equal
+    bits); the fixed-peer kernel adds into dk and dv atomically (order not
+    fixed), so those are compared to within fp32 rounding."""
+    from tarmac_b200 import autograd as ag
+
+    def fn(q, k, v):
+        return ag.topk_attention(q, k, v, 2) if op == "topk" else ag.dense_attention(q, k, v)
+
+    B, N, d = 256, 6, 16
+    sample = [t.requires_grad_(True) for t in _inputs(B, N, d, 11)]
+    graphed = torch.cuda.make_graphed_callables(fn, tuple(sample))
+    for seed in (12, 13):
+        x = [t.requires_grad_(True) for t in _inputs(B, N, d, seed)]
+        go = _inputs(B, N, d, seed + 100)[0]
+        out = graphed(*x)
+        got = torch.autograd.grad(out, x, go)
+        y = [t.detach().clone().requires_grad_(True) for t in x]
+        ref_out = fn(*y)
+        want = torch.autograd.grad(ref_out, y, go)
+        assert torch.equal(out, ref_out)
+        for a, b in zip(got, want):
+            if op == "dense":
+                assert torch.equal(a, b)
+            else:
+                torch.testing.assert_close(a, b, rtol=1e-5, atol=1e-6)
