@@ -69,8 +69,9 @@ cudaError_t launch_topk_ws(const AttnParams& p, int dtype, bool tie_high,
 // k <= 8 with the lowest- or highest-index tie rule: episodes of 128 agents
 // or more (from 65 for k <= 4, from 96 for k <= 8) form their scores on the
 // tensor cores (bf16 directly; fp32 as three exact bf16 planes, d a
-// multiple of 8 up to 16, 16-byte rows) — large batches of 385-512-agent
-// episodes in the persistent warp-specialized kernel (topk_ws.cu) where it
+// multiple of 8 up to 16, 16-byte rows) — batches of at least one (bf16) or
+// two (fp32) episodes per SM of 320-512 (bf16) or 352-512 (fp32) agents in
+// the persistent warp-specialized kernel (topk_ws.cu) where it
 // measured faster, others one 128-query block at a time (topk_tc.cu); both
 // return the same bits. Other episodes up to 128 agents with d <= 16 run
 // one or two lanes per query row (topk_small.cu); otherwise the chunked

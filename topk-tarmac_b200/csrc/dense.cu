@@ -249,7 +249,8 @@ bool dense_ws_supported(const AttnParams& p);
 cudaError_t launch_dense_ws(const AttnParams& p, cudaStream_t s);
 
 // Episodes of 128 or more agents run on the tensor cores: bf16 directly —
-// large batches of 385-512-agent episodes with d from 24 to 64 in the
+// batches of at least four episodes per SM of 320-512 agents with d from 24
+// to 64 in the
 // persistent warp-specialized kernel (dense_ws.cu), others one 128-query
 // block at a time (dense_tc.cu), the same bits either way — and fp32 with d
 // in {8, 16} and 16-byte rows as three exact bf16 planes; other shapes on
