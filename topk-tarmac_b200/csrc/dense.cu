@@ -250,9 +250,8 @@ cudaError_t launch_dense_ws(const AttnParams& p, cudaStream_t s);
 
 // Episodes of 128 or more agents run on the tensor cores: bf16 directly —
 // batches of at least four episodes per SM of 320-512 agents with d from 24
-// to 64 in the
-// persistent warp-specialized kernel (dense_ws.cu), others one 128-query
-// block at a time (dense_tc.cu), the same bits either way — and fp32 with d
+// to 64 in the persistent warp-specialized kernel (dense_ws.cu), others one
+// 128-query block at a time (dense_tc.cu), the same bits either way — and fp32 with d
 // in {8, 16} and 16-byte rows as three exact bf16 planes; other shapes on
 // the packed-FMA kernel above.
 // 0: persistent warp-specialized, 1: tensor-core per block (bf16), 2:
