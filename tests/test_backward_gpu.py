@@ -44,6 +44,28 @@ def test_dense_backward(tb, N, d):
         close(a, b)
 
 
+@pytest.mark.parametrize("N,d,scale_in,strided", [
+    (128, 16, 1.0, False), (129, 16, 1.0, False), (1000, 16, 1.0, False),
+    (256, 16, 6.0, False), (300, 16, 1.0, True)])
+def test_dense_backward_tensor_cores(tb, N, d, scale_in, strided):
+    """fp32 with d = 16 and at least 128 agents: the tensor-core kernels
+    (backward_tc.cu), partial tiles, large scores (the log-sum-exp's
+    reference point moves) and strided views included."""
+    ops, _ = tb
+    if strided:
+        base = qkv(3, N, 3 * d, seed=N + 7)[0]
+        q, k, v = base[..., :d], base[..., d:2 * d], base[..., 2 * d:]
+    else:
+        q, k, v = qkv(3, N, d, seed=N * 11 + d)
+        q = q * scale_in
+    g = torch.randn(3, N, d, generator=torch.Generator().manual_seed(N + 1)).cuda()
+    out = ops.dense_attention(q, k, v)
+    dq, dk, dv = ops.dense_attention_backward(q, k, v, out, g)
+    want = oracle.dense_attention_grad(host(q), host(k), host(v), host(g))
+    for a, b in zip((dq, dk, dv), want):
+        close(a, b)
+
+
 @pytest.mark.parametrize("N,d", [(6, 16), (128, 16), (300, 32), (512, 64)])
 def test_dense_backward_bf16(tb, N, d):
     """bf16 inputs (fp32 arithmetic on the widened values); D from the

@@ -414,7 +414,12 @@ static cudaError_t launch_dense_bwd_dt(const BwdParams& p, cudaStream_t s) {
   return launch_dense_bwd_t<128, T>(p, s);
 }
 
+bool dense_bwd_tc_supported(const BwdParams& p, int bf16);
+cudaError_t launch_dense_bwd_tc(const BwdParams& p, cudaStream_t s);
+
 cudaError_t launch_dense_bwd(const BwdParams& p, int bf16, cudaStream_t s) {
+  // fp32, d = 16, N >= 128: the tensor-core kernels (backward_tc.cu)
+  if (dense_bwd_tc_supported(p, bf16)) return launch_dense_bwd_tc(p, s);
   return bf16 ? launch_dense_bwd_dt<__nv_bfloat16>(p, s)
               : launch_dense_bwd_dt<float>(p, s);
 }
