@@ -5,8 +5,10 @@
 
 Inputs are seeded i.i.d. N(0, 1) Q, K, V (positions U[0, 1)^2 for the
 Morton ops; for the comm module, x rows of width --in_dim and its
-weights with message width --d), drawn on the CPU and copied to the device
-once; every repetition is one launch of the selected operation on the current stream.
+weights with message width --d; for the gradient ops dense_bwd and
+topk_bwd, an N(0, 1) dO and the forward's output or retained peers), drawn
+on the CPU and copied to the device once; every repetition is one call of
+the selected operation on the current stream.
 Prints "ok" and the mean per-call time (CUDA events) on success.
 """
 
@@ -25,7 +27,7 @@ def main() -> int:
     ap.add_argument("--op", default="topk",
                     choices=("topk", "topk_sort", "topk_threshold", "stream",
                              "dense", "morton_prescore", "morton_select",
-                             "prescore", "comm"))
+                             "prescore", "comm", "dense_bwd", "topk_bwd"))
     ap.add_argument("--B", type=int, default=1024)
     ap.add_argument("--N", type=int, default=512)
     ap.add_argument("--d", type=int, default=16)
@@ -56,6 +58,13 @@ def main() -> int:
         bq = (0.1 * torch.randn(3 * a.d, generator=g)).cuda()
         wp = (torch.randn(a.d, a.d, generator=g) / a.d ** 0.5).cuda()
         bp = (0.1 * torch.randn(a.d, generator=g)).cuda()
+    # gradient ops: dO and the forward's output (dense) or retained peers
+    # (top-k), computed once before the timed calls
+    if a.op in ("dense_bwd", "topk_bwd"):
+        go = torch.randn(a.B, a.N, a.d, generator=g).to(dt).cuda()
+        o_d = ops.dense_attention(q, k, v) if a.op == "dense_bwd" else None
+        idx = (ops.topk_attention(q, k, v, a.k, return_indices=True)[1]
+               if a.op == "topk_bwd" else None)
     calls = {
         "topk": lambda: ops.topk_attention(q, k, v, a.k),
         "topk_sort": lambda: ops.topk_attention(q, k, v, a.k, mode="sort"),
@@ -68,6 +77,8 @@ def main() -> int:
         "morton_select": lambda: ops.morton_select(pos, a.k, bits=a.bits),
         "prescore": lambda: ops.prescore_attention(q, k, v, widx),
         "comm": lambda: ops.comm_forward(x, wq, bq, wp, bp, a.k),
+        "dense_bwd": lambda: ops.dense_attention_backward(q, k, v, o_d, go),
+        "topk_bwd": lambda: ops.gather_attention_backward(q, k, v, go, idx),
     }
     fn = calls[a.op]
     fn()
