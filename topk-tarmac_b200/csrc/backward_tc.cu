@@ -1,7 +1,7 @@
 // backward_tc.cu — gradients of dense masked-diagonal attention on the
 // tensor cores, for fp32 inputs with d = 16 (the message width of the
-// reference's comm module) and at least 128 agents: the same gradients as the FFMA kernels of
-// backward.cu (the reference trains its eager dense path,
+// reference's comm module) and at least 128 agents: the same gradients as
+// the FFMA kernels of backward.cu (the reference trains its eager dense path,
 // src/agents/mappo.py:361-373, through autograd), with every product
 // formed as the six bf16 plane products of the exact three-plane split of
 // its fp32 operands (tc_common.cuh:split3_bf16x2), small terms first, as
@@ -33,7 +33,7 @@ namespace tarmac {
 
 constexpr int BTC_THREADS = 256;  // two threads per row, 32 columns of a tile each
 constexpr int BTC_TILE = 64;   // keys (dq kernel) or queries (dk/dv kernel) per tile
-constexpr int BTC_DP = 16;     // padded head width
+constexpr int BTC_DP = 16;     // head width
 constexpr float BTC_LOG2E = 1.4426950408889634f;
 constexpr float BTC_RESCALE_LOG2 = 8.0f;
 // plane products, small terms first: m.m, l.h, h.l, m.h, h.m, h.h
@@ -167,12 +167,14 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dq_kernel(BwdPara
   const int tiles = cdiv(N, BTC_TILE);
   unsigned char* wrow = sW + (row >> 3) * WCH * 128 + (row & 7) * 16;
 
-  // pass 1: row log-sum-exp (base 2) over the keys j != i; the reference
-  // point moves only when a score exceeds it by more than 2^8
-  // the next tile's rows are loaded into registers while the current one
-  // is in the products and the exponentials
+  // The next tile's rows are loaded into registers while the current one
+  // is in the products and the exponentials (first 128 threads).
   tc::SplitTile<BTC_DP, BTC_TILE, false> kt, vt;
   tc::SplitTile<BTC_DP, BTC_TILE, true> kmt;
+
+  // pass 1: row log-sum-exp (base 2) over the keys j != i, each thread over
+  // its 32 columns of every tile; the reference point moves only when a
+  // score exceeds it by more than 2^8
   float mref = -INFINITY, sum = 0.f;
   if (stager) kt.load(K, p.kn, N, d);
   for (int j = 0; j < tiles; ++j) {
