@@ -97,6 +97,18 @@ __device__ __forceinline__ void store_weights32(unsigned char* wrow, int h,
   }
 }
 
+// Scores of columns [c0, c0 + 32) of row r (one of the warp's rows
+// [r0, r0 + 32)) set to -inf where they must not count: the diagonal,
+// columns past N, and every column of a padding row (r >= N). Warp-uniform
+// test: only tiles that hold the warp's diagonal or padding are touched.
+__device__ __forceinline__ void mask_edge(float (&s)[32], int c0, int r0, int r, int N) {
+  if (c0 + 32 > N || r0 + 32 > N || (c0 < r0 + 32 && r0 < c0 + 32)) {
+#pragma unroll
+    for (int t = 0; t < 32; ++t)
+      if (c0 + t >= N || c0 + t == r || r >= N) s[t] = -INFINITY;
+  }
+}
+
 __device__ __forceinline__ void sync_smem_for_mma() {
   tc::fence_async_smem();
   tc::fence_before_sync();
@@ -175,7 +187,8 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dq_kernel(BwdPara
   // pass 1: row log-sum-exp (base 2) over the keys j != i, each thread over
   // its 32 columns of every tile; the reference point moves only when a
   // score exceeds it by more than 2^8
-  float mref = -INFINITY, sum = 0.f;
+  // the reference starts finite, so a masked score (-inf) adds 2^-inf = 0
+  float mref = -1e30f, sum = 0.f;
   if (stager) kt.load(K, p.kn, N, d);
   for (int j = 0; j < tiles; ++j) {
     const int k0 = j * BTC_TILE;
@@ -193,17 +206,15 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dq_kernel(BwdPara
     {
       float s[32];
       tc::tmem_ld32(t_s + lane_off + cb, s);
+      mask_edge(s, k0 + cb, q0 + wq * 32, i, N);
 #pragma unroll
       for (int t = 0; t < 32; ++t) {
-        const int kj = k0 + cb + t;
-        if (kj < N && kj != i) {
-          const float x = s[t] * c2;
-          if (x > mref + BTC_RESCALE_LOG2) {
-            sum *= btc::ex2(mref - x);
-            mref = x;
-          }
-          sum += btc::ex2(x - mref);
+        const float x = s[t] * c2;
+        if (x > mref + BTC_RESCALE_LOG2) {
+          sum *= btc::ex2(mref - x);
+          mref = x;
         }
+        sum += btc::ex2(x - mref);
       }
     }
     tc::fence_before_sync();
@@ -217,8 +228,8 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dq_kernel(BwdPara
   {
     const float mo = red_m[half ^ 1][row], so = red_s[half ^ 1][row];
     const float m = fmaxf(mref, mo);
-    lse2 = m == -INFINITY ? -INFINITY
-                          : m + log2f(sum * btc::ex2(mref - m) + so * btc::ex2(mo - m));
+    lse2 = m + log2f(sum * btc::ex2(mref - m) + so * btc::ex2(mo - m));
+    if (i >= N) lse2 = 0.f;  // a padding row: every score is masked below
   }
 
   // pass 2: dS and dQ
@@ -250,13 +261,9 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dq_kernel(BwdPara
       float s[32], dp[32];
       tc::tmem_ld32(t_s + lane_off + cb, s);
       tc::tmem_ld32(t_dp + lane_off + cb, dp);
+      mask_edge(s, k0 + cb, q0 + wq * 32, i, N);
 #pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        const int kj = k0 + cb + t;
-        const bool live = i < N && kj < N && kj != i;
-        const float pw = live ? btc::ex2(fmaf(s[t], c2, -lse2)) : 0.f;
-        s[t] = pw * (dp[t] - D);
-      }
+      for (int t = 0; t < 32; ++t) s[t] = btc::ex2(fmaf(s[t], c2, -lse2)) * (dp[t] - D);
       store_weights32(wrow, half, s);
     }
     sync_smem_for_mma();
@@ -385,12 +392,9 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dkdv_kernel(BwdPa
     {
       float s[32];
       tc::tmem_ld32(t_s + lane_off + cb, s);
+      mask_edge(s, i0 + cb, j0 + wq * 32, jr, N);
 #pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        const int qi = i0 + cb + t;
-        const bool live = jr < N && qi < N && qi != jr;
-        s[t] = live ? btc::ex2(fmaf(s[t], c2, -slse[cb + t])) : 0.f;
-      }
+      for (int t = 0; t < 32; ++t) s[t] = btc::ex2(fmaf(s[t], c2, -slse[cb + t]));
       store_weights32(wrow, half, s);
     }
     sync_smem_for_mma();
@@ -404,13 +408,10 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dkdv_kernel(BwdPa
       float s[32], dp[32];
       tc::tmem_ld32(t_s + lane_off + cb, s);
       tc::tmem_ld32(t_dp + lane_off + cb, dp);
+      mask_edge(s, i0 + cb, j0 + wq * 32, jr, N);
 #pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        const int qi = i0 + cb + t;
-        const bool live = jr < N && qi < N && qi != jr;
-        const float pw = live ? btc::ex2(fmaf(s[t], c2, -slse[cb + t])) : 0.f;
-        s[t] = pw * (dp[t] - sD[cb + t]);
-      }
+      for (int t = 0; t < 32; ++t)
+        s[t] = btc::ex2(fmaf(s[t], c2, -slse[cb + t])) * (dp[t] - sD[cb + t]);
       store_weights32(wrow, half, s);
     }
     sync_smem_for_mma();
