@@ -207,15 +207,17 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dq_kernel(BwdPara
       float s[32];
       tc::tmem_ld32(t_s + lane_off + cb, s);
       mask_edge(s, k0 + cb, q0 + wq * 32, i, N);
+      // the reference moves at most once a tile, to the tile's maximum
+      float mt = s[0];
 #pragma unroll
-      for (int t = 0; t < 32; ++t) {
-        const float x = s[t] * c2;
-        if (x > mref + BTC_RESCALE_LOG2) {
-          sum *= btc::ex2(mref - x);
-          mref = x;
-        }
-        sum += btc::ex2(x - mref);
+      for (int t = 1; t + 1 < 32; t += 2) mt = max3f(mt, s[t], s[t + 1]);
+      mt = fmaxf(mt, s[31]) * c2;
+      if (mt > mref + BTC_RESCALE_LOG2) {
+        sum *= btc::ex2(mref - mt);
+        mref = mt;
       }
+#pragma unroll
+      for (int t = 0; t < 32; ++t) sum += btc::ex2(fmaf(s[t], c2, -mref));
     }
     tc::fence_before_sync();
     __syncthreads();  // S read by every thread before the next product
@@ -388,15 +390,13 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dkdv_kernel(BwdPa
       tc::mma_commit(&mbar);
     }
     wait_products();
-    // P^T for dV
-    {
-      float s[32];
-      tc::tmem_ld32(t_s + lane_off + cb, s);
-      mask_edge(s, i0 + cb, j0 + wq * 32, jr, N);
+    // P^T for dV; the weights stay in registers for dS^T
+    float pw[32];
+    tc::tmem_ld32(t_s + lane_off + cb, pw);
+    mask_edge(pw, i0 + cb, j0 + wq * 32, jr, N);
 #pragma unroll
-      for (int t = 0; t < 32; ++t) s[t] = btc::ex2(fmaf(s[t], c2, -slse[cb + t]));
-      store_weights32(wrow, half, s);
-    }
+    for (int t = 0; t < 32; ++t) pw[t] = btc::ex2(fmaf(pw[t], c2, -slse[cb + t]));
+    store_weights32(wrow, half, pw);
     sync_smem_for_mma();
     if (threadIdx.x == 0) {
       mma_weights_x_tile(t_dv, wa, gma, it > 0);
@@ -405,14 +405,11 @@ __global__ void __launch_bounds__(BTC_THREADS, 2) dense_bwd_tc_dkdv_kernel(BwdPa
     wait_products();  // P^T read: the weight tile takes dS^T next
     // dS^T for dK
     {
-      float s[32], dp[32];
-      tc::tmem_ld32(t_s + lane_off + cb, s);
+      float dp[32];
       tc::tmem_ld32(t_dp + lane_off + cb, dp);
-      mask_edge(s, i0 + cb, j0 + wq * 32, jr, N);
 #pragma unroll
-      for (int t = 0; t < 32; ++t)
-        s[t] = btc::ex2(fmaf(s[t], c2, -slse[cb + t])) * (dp[t] - sD[cb + t]);
-      store_weights32(wrow, half, s);
+      for (int t = 0; t < 32; ++t) pw[t] *= dp[t] - sD[cb + t];
+      store_weights32(wrow, half, pw);
     }
     sync_smem_for_mma();
     if (threadIdx.x == 0) {
